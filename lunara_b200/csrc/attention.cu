@@ -1,0 +1,509 @@
+// Scaled-dot-product attention forward, O = softmax(Q K^T * scale [+ causal]) V.
+//
+// tcgen05 path (f16 / bf16, D == 64): FlashAttention-style single pass with an
+// online softmax. One CTA owns 256 query rows of one (batch, head) as two
+// 128-row Q tiles, each with its own softmax warpgroup so that the tensor core
+// works on one tile while the other tile's softmax runs (ping-pong):
+//   warps 0-3   softmax warpgroup 0 (thread = query row of Q tile 0)
+//   warps 4-7   softmax warpgroup 1 (Q tile 1)
+//   warp 8      TMA producer: Q tiles once, K and V [128 x 64] blocks into a
+//               3-deep ring (128-byte swizzle, 4-D tensor maps over the
+//               caller's strides, so a fused QKV buffer is read in place)
+//   warp 9      TMEM allocator + single-thread tcgen05.mma issuer
+//                 S_w = Q_w K_j^T   (M=128, N=128, K=64)   -> TMEM
+//                 O_w = P_w V_j     (M=128, N=64,  K=128)  -> TMEM
+// The softmax warps read S from TMEM twice (row max, then exp2 + row sum),
+// write P as fp16/bf16 into a swizzled K-major shared tile for the PV MMA, and
+// fold each P V block into a register accumulator with the running rescale.
+// Causal masking skips key blocks above the diagonal and masks the diagonal
+// block; heavy query blocks are scheduled first.
+// SIMT path: any D <= 256, any dtype, one warp per query row.
+//
+// Semantics follow lunara/codegen/triton_emitter.py:212-293: scale applied to
+// Q K^T (launcher passes 1/sqrt(D), 302), causal keep-mask row >= col
+// (265-268), fp32 softmax and accumulation. Keys past the end of the sequence
+// are excluded from the softmax (the reference loads them as zeros and lets
+// them take part, which only matters when Skv is not a multiple of its block).
+#include <cudaTypedefs.h>
+
+#include <type_traits>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace lunara {
+namespace {
+
+constexpr int kQTile = 128;     // query rows per softmax warpgroup
+constexpr int kKvBlock = 128;   // keys per iteration
+constexpr int kHeadDim = 64;
+constexpr int kKvStages = 3;
+constexpr int kAttnThreads = 320;
+constexpr uint32_t kTileBytes = 128 * 128;  // one [128 x 64] 16-bit tile
+constexpr int kAttnSmem = 2 * kTileBytes + 2 * kKvStages * kTileBytes + 2 * 2 * kTileBytes + 256 + 1024;
+constexpr uint32_t kAttnTmemCols = 512;
+
+struct AttnParams {
+  void* O;
+  int64_t os_b, os_h, os_s;
+  int H, Sq, Skv;
+  int n_qblocks;
+  float scale_log2;
+  int causal;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                   const __grid_constant__ CUtensorMap tv, const AttnParams p, unsigned int* err) {
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t IDESC_S = idesc_f16(128, kKvBlock, kBF16, false, false);
+  constexpr uint32_t IDESC_PV = idesc_f16(128, kHeadDim, kBF16, false, true);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
+  uint8_t* sQ = smem;                                   // 2 tiles
+  uint8_t* sK = sQ + 2 * kTileBytes;                    // kKvStages tiles
+  uint8_t* sV = sK + kKvStages * kTileBytes;            // kKvStages tiles
+  uint8_t* sP = sV + kKvStages * kTileBytes;            // 2 x (2 tiles)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 4 * kTileBytes);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + kKvStages;
+  uint64_t* v_full = k_empty + kKvStages;
+  uint64_t* v_empty = v_full + kKvStages;
+  uint64_t* s_full = v_empty + kKvStages;   // [2]
+  uint64_t* p_ready = s_full + 2;           // [2]
+  uint64_t* o_full = p_ready + 2;           // [2]
+  uint64_t* drain_bar = o_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int qb = p.causal ? (p.n_qblocks - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int q0 = qb * 2 * kQTile;
+  const int nb_total = (p.Skv + kKvBlock - 1) / kKvBlock;
+  // Key blocks each Q tile visits (0 for a tile past the end of the sequence).
+  auto blocks_for = [&](int first) {
+    if (first >= p.Sq) return 0;
+    if (!p.causal) return nb_total;
+    const int lim = (first + kQTile - 1) / kKvBlock + 1;
+    return lim < nb_total ? lim : nb_total;
+  };
+  const int nb0 = blocks_for(q0);
+  const int nb1 = blocks_for(q0 + kQTile);
+  const int nb = nb0 > nb1 ? nb0 : nb1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kKvStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(&s_full[w], 1);
+      mbar_init(&p_ready[w], kQTile);
+      mbar_init(&o_full[w], 1);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, kAttnTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 8) {
+    if (lane == 0) {
+      // -------------------------------------------------------- TMA producer --
+      tma_prefetch_desc(&tq);
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
+      tma_load_4d(sQ, &tq, q_full, 0, q0, h, b);
+      tma_load_4d(sQ + kTileBytes, &tq, q_full, 0, q0 + kQTile, h, b);
+      int issued_k = 0, issued_v = 0;
+      bool ok = true;
+      for (int j = 0; j < nb && ok; ++j) {
+        const int st = j % kKvStages;
+        const uint32_t ph = static_cast<uint32_t>(j / kKvStages) & 1u;
+        if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, err, kErrAttnProducer)) { ok = false; break; }
+        mbar_arrive_expect_tx(&k_full[st], kTileBytes);
+        tma_load_4d(sK + st * kTileBytes, &tk, &k_full[st], 0, j * kKvBlock, h, b);
+        ++issued_k;
+        if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, err, kErrAttnProducer)) { ok = false; break; }
+        mbar_arrive_expect_tx(&v_full[st], kTileBytes);
+        tma_load_4d(sV + st * kTileBytes, &tv, &v_full[st], 0, j * kKvBlock, h, b);
+        ++issued_v;
+      }
+      if (!ok) {
+        mbar_drain_wait(q_full, 0, 1000000000ull);
+        for (int i = (issued_k > kKvStages ? issued_k - kKvStages : 0); i < issued_k; ++i)
+          mbar_drain_wait(&k_full[i % kKvStages], static_cast<uint32_t>(i / kKvStages) & 1u, 1000000000ull);
+        for (int i = (issued_v > kKvStages ? issued_v - kKvStages : 0); i < issued_v; ++i)
+          mbar_drain_wait(&v_full[i % kKvStages], static_cast<uint32_t>(i / kKvStages) & 1u, 1000000000ull);
+      }
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- MMA issuer --
+      bool ok = mbar_wait(q_full, 0, abort_flag, err, kErrAttnMma);
+      if (ok && nb > 0) {
+        tc_fence_after();
+        const uint32_t q_base = smem_u32(sQ);
+        const uint32_t p_base = smem_u32(sP);
+        auto issue_s = [&](int w, int st) {
+          const uint32_t q_addr = q_base + w * kTileBytes;
+          const uint32_t k_addr = smem_u32(sK + st * kTileBytes);
+#pragma unroll
+          for (int k = 0; k < kHeadDim / 16; ++k)
+            umma_f16_ss(tmem_base + w * 128, sw128_desc(q_addr + k * 32, 16, 1024),
+                        sw128_desc(k_addr + k * 32, 16, 1024), IDESC_S, k > 0 ? 1u : 0u);
+        };
+        auto issue_pv = [&](int w, int st) {
+          const uint32_t p_addr = p_base + w * 2 * kTileBytes;
+          const uint32_t v_addr = smem_u32(sV + st * kTileBytes);
+#pragma unroll
+          for (int k = 0; k < kKvBlock / 16; ++k)
+            umma_f16_ss(tmem_base + 256 + w * 128,
+                        sw128_desc(p_addr + (k / 4) * kTileBytes + (k % 4) * 32, 16, 1024),
+                        sw128_desc(v_addr + k * 2048, kTileBytes, 1024), IDESC_PV, k > 0 ? 1u : 0u);
+        };
+        ok = mbar_wait(&k_full[0], 0, abort_flag, err, kErrAttnMma);
+        if (ok) {
+          tc_fence_after();
+          for (int w = 0; w < 2; ++w) {
+            if ((w ? nb1 : nb0) > 0) {
+              issue_s(w, 0);
+              umma_commit(&s_full[w]);
+            }
+          }
+          umma_commit(&k_empty[0]);
+        }
+        for (int j = 0; j < nb && ok; ++j) {
+          const int st = j % kKvStages;
+          const uint32_t ph = static_cast<uint32_t>(j / kKvStages) & 1u;
+          const bool has_next = j + 1 < nb;
+          const int st1 = (j + 1) % kKvStages;
+          const uint32_t ph1 = static_cast<uint32_t>((j + 1) / kKvStages) & 1u;
+          if (!mbar_wait(&v_full[st], ph, abort_flag, err, kErrAttnMma)) { ok = false; break; }
+          if (has_next && !mbar_wait(&k_full[st1], ph1, abort_flag, err, kErrAttnMma)) { ok = false; break; }
+          for (int w = 0; w < 2 && ok; ++w) {
+            const int nbw = w ? nb1 : nb0;
+            if (j >= nbw) continue;
+            if (!mbar_wait(&p_ready[w], static_cast<uint32_t>(j) & 1u, abort_flag, err, kErrAttnMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(w, st);
+            umma_commit(&o_full[w]);
+            if (j + 1 < nbw) {
+              issue_s(w, st1);
+              umma_commit(&s_full[w]);
+            }
+          }
+          if (!ok) break;
+          umma_commit(&v_empty[st]);
+          if (has_next) umma_commit(&k_empty[st1]);
+        }
+      }
+      if (!ok) {
+        umma_commit(drain_bar);
+        mbar_drain_wait(drain_bar, 0, 1000000000ull);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- softmax --
+    const int w = warp >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int qrow = q0 + w * kQTile + r;
+    const int q_first = q0 + w * kQTile;
+    const int my_nb = w ? nb1 : nb0;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tS = tmem_base + lane_off + w * 128;
+    const uint32_t tO = tmem_base + lane_off + 256 + w * 128;
+    uint8_t* myP = sP + w * 2 * kTileBytes;
+    const float sl2 = p.scale_log2;
+    float m = -INFINITY, l = 0.f, alpha_pend = 0.f;
+    float o[kHeadDim];
+#pragma unroll
+    for (int i = 0; i < kHeadDim; ++i) o[i] = 0.f;
+    bool ok = true;
+
+    for (int j = 0; j < my_nb; ++j) {
+      if (!mbar_wait(&s_full[w], static_cast<uint32_t>(j) & 1u, abort_flag, err, kErrAttnSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int kv0 = j * kKvBlock;
+      const bool need_mask = (kv0 + kKvBlock > p.Skv) || (p.causal && kv0 + kKvBlock - 1 > q_first);
+      // Pass 1: row maximum of the scores.
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kKvBlock / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tS + c * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float s = __uint_as_float(v[i]);
+          if (need_mask) {
+            const int col = kv0 + c * 32 + i;
+            if (col >= p.Skv || (p.causal && col > qrow)) s = -INFINITY;
+          }
+          mx = fmaxf(mx, s);
+        }
+      }
+      const float m_new = fmaxf(m, mx * sl2);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = ex2_approx(m - m_use);
+      // The previous P V product must be done before P is overwritten; fold it in.
+      if (j > 0) {
+        if (!mbar_wait(&o_full[w], static_cast<uint32_t>(j - 1) & 1u, abort_flag, err, kErrAttnSoftmax)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < kHeadDim / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tO + c * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha_pend, __uint_as_float(v[i]));
+        }
+      }
+      // Pass 2: P = exp2(S * scale * log2e - m), row sum, P -> swizzled smem.
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < kKvBlock / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tS + c * 32, v);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float s0 = __uint_as_float(v[i]), s1 = __uint_as_float(v[i + 1]);
+          if (need_mask) {
+            const int col = kv0 + c * 32 + i;
+            if (col >= p.Skv || (p.causal && col > qrow)) s0 = -INFINITY;
+            if (col + 1 >= p.Skv || (p.causal && col + 1 > qrow)) s1 = -INFINITY;
+          }
+          const float e0 = ex2_approx(fmaf(s0, sl2, -m_use));
+          const float e1 = ex2_approx(fmaf(s1, sl2, -m_use));
+          sum += e0 + e1;
+          pk[i / 2] = Io<T>::pack2(e0, e1);
+        }
+        uint8_t* chunk = myP + (c / 2) * kTileBytes + r * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int u = (c % 2) * 4 + q;
+          *reinterpret_cast<uint4*>(chunk + ((u ^ (r & 7)) * 16)) =
+              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        }
+      }
+      l = fmaf(l, alpha, sum);
+      m = m_new;
+      alpha_pend = alpha;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_ready[w]);
+    }
+    if (ok && my_nb > 0) {
+      if (mbar_wait(&o_full[w], static_cast<uint32_t>(my_nb - 1) & 1u, abort_flag, err, kErrAttnSoftmax)) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < kHeadDim / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tO + c * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha_pend, __uint_as_float(v[i]));
+        }
+        if (qrow < p.Sq) {
+          const float inv_l = 1.0f / l;
+          T* out = static_cast<T*>(p.O) + b * p.os_b + h * p.os_h + static_cast<int64_t>(qrow) * p.os_s;
+          uint4* ov = reinterpret_cast<uint4*>(out);
+#pragma unroll
+          for (int q = 0; q < kHeadDim / 8; ++q) {
+            uint4 u;
+            u.x = Io<T>::pack2(o[8 * q + 0] * inv_l, o[8 * q + 1] * inv_l);
+            u.y = Io<T>::pack2(o[8 * q + 2] * inv_l, o[8 * q + 3] * inv_l);
+            u.z = Io<T>::pack2(o[8 * q + 4] * inv_l, o[8 * q + 5] * inv_l);
+            u.w = Io<T>::pack2(o[8 * q + 6] * inv_l, o[8 * q + 7] * inv_l);
+            ov[q] = u;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kAttnTmemCols);
+  }
+}
+
+// ------------------------------------------------------------ SIMT path ----
+// One warp per query row; lane holds D/32 (<= 8) elements of q and o.
+template <typename T>
+__global__ void __launch_bounds__(128) attn_simt_kernel(const T* __restrict__ Q, const T* __restrict__ K,
+                                                        const T* __restrict__ V, T* __restrict__ O, AttnArgs a) {
+  const int64_t qi = static_cast<int64_t>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int64_t h = blockIdx.y, b = blockIdx.z;
+  if (qi >= a.Sq) return;
+  constexpr int kMaxPer = 8;
+  const int per = static_cast<int>((a.D + 31) / 32);
+  const T* q = Q + b * a.qs[0] + h * a.qs[1] + qi * a.qs[2];
+  float qv[kMaxPer], ov[kMaxPer];
+#pragma unroll
+  for (int e = 0; e < kMaxPer; ++e) {
+    const int64_t d = lane + 32 * e;
+    qv[e] = (e < per && d < a.D) ? Io<T>::to_f(q[d * a.qs[3]]) * a.scale : 0.f;
+    ov[e] = 0.f;
+  }
+  float m = -INFINITY, l = 0.f;
+  const int64_t kend = a.causal ? (qi + 1 < a.Skv ? qi + 1 : a.Skv) : a.Skv;
+  for (int64_t j = 0; j < kend; ++j) {
+    const T* k = K + b * a.ks[0] + h * a.ks[1] + j * a.ks[2];
+    const T* v = V + b * a.vs[0] + h * a.vs[1] + j * a.vs[2];
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < kMaxPer; ++e) {
+      const int64_t d = lane + 32 * e;
+      if (e < per && d < a.D) s = fmaf(qv[e], Io<T>::to_f(k[d * a.ks[3]]), s);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float m_new = fmaxf(m, s);
+    const float corr = __expf(m - m_new);
+    const float pj = __expf(s - m_new);
+    l = l * corr + pj;
+#pragma unroll
+    for (int e = 0; e < kMaxPer; ++e) {
+      const int64_t d = lane + 32 * e;
+      if (e < per && d < a.D) ov[e] = fmaf(ov[e], corr, pj * Io<T>::to_f(v[d * a.vs[3]]));
+    }
+    m = m_new;
+  }
+  T* out = O + b * a.os[0] + h * a.os[1] + qi * a.os[2];
+  const float inv = 1.0f / l;
+#pragma unroll
+  for (int e = 0; e < kMaxPer; ++e) {
+    const int64_t d = lane + 32 * e;
+    if (e < per && d < a.D) out[d * a.os[3]] = Io<T>::from_f(ov[e] * inv);
+  }
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool encode_4d(CUtensorMap* map, const void* base, int dtype, int64_t S, int64_t H, int64_t B, const int64_t* st) {
+  auto encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(tensor_map_encoder());
+  if (encode == nullptr) return false;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(kHeadDim), static_cast<cuuint64_t>(S),
+                              static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(B)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(st[2] * 2), static_cast<cuuint64_t>(st[1] * 2),
+                                 static_cast<cuuint64_t>(st[0] * 2)};
+  const cuuint32_t box[4] = {kHeadDim, 128, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt =
+      dtype == LUNARA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return encode(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool strides_ok(const int64_t* s) {
+  // dim stride 1; batch/head/seq strides give 16-byte aligned rows and fit TMA's 40-bit stride field.
+  if (s[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if (s[i] < 0 || (s[i] * 2) % 16 != 0 || s[i] * 2 >= (int64_t{1} << 40)) return false;
+  return true;
+}
+
+template <typename T>
+cudaError_t run_tc(const AttnArgs& a, cudaStream_t s) {
+  CUtensorMap mq, mk, mv;
+  if (!encode_4d(&mq, a.Q, a.dtype, a.Sq, a.H, a.B, a.qs) || !encode_4d(&mk, a.K, a.dtype, a.Skv, a.H, a.B, a.ks) ||
+      !encode_4d(&mv, a.V, a.dtype, a.Skv, a.H, a.B, a.vs))
+    return cudaErrorInvalidValue;
+  auto kern = attn_tc_kernel<T>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+  if (e != cudaSuccess) return e;
+  AttnParams p{};
+  p.O = a.O;
+  p.os_b = a.os[0];
+  p.os_h = a.os[1];
+  p.os_s = a.os[2];
+  p.H = static_cast<int>(a.H);
+  p.Sq = static_cast<int>(a.Sq);
+  p.Skv = static_cast<int>(a.Skv);
+  p.n_qblocks = static_cast<int>(ceil_div64(a.Sq, 2 * kQTile));
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.causal = a.causal;
+  unsigned int* err = device_error_word();
+  if (err == nullptr) return cudaErrorInvalidDevice;
+  const dim3 grid(static_cast<unsigned>(p.n_qblocks), static_cast<unsigned>(a.H), static_cast<unsigned>(a.B));
+  kern<<<grid, kAttnThreads, kAttnSmem, s>>>(mq, mk, mv, p, err);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool attention_tc_supported(const AttnArgs& a) {
+  if (a.dtype != LUNARA_F16 && a.dtype != LUNARA_BF16) return false;
+  if (a.D != kHeadDim) return false;
+  if (a.Sq < 1 || a.Skv < 1 || a.Sq >= (int64_t{1} << 30) || a.Skv >= (int64_t{1} << 30)) return false;
+  if (a.H > 65535 || a.B > 65535) return false;
+  if (!al16(a.Q) || !al16(a.K) || !al16(a.V) || !al16(a.O)) return false;
+  if (!strides_ok(a.qs) || !strides_ok(a.ks) || !strides_ok(a.vs) || !strides_ok(a.os)) return false;
+  return true;
+}
+
+cudaError_t launch_attention_tcgen05(const AttnArgs& a, cudaStream_t stream) {
+  return a.dtype == LUNARA_BF16 ? run_tc<__nv_bfloat16>(a, stream) : run_tc<__half>(a, stream);
+}
+
+cudaError_t launch_attention_simt(const AttnArgs& a, cudaStream_t stream) {
+  if (a.Sq == 0 || a.B == 0 || a.H == 0) return cudaSuccess;
+  const dim3 grid(static_cast<unsigned>(ceil_div64(a.Sq, 4)), static_cast<unsigned>(a.H),
+                  static_cast<unsigned>(a.B));
+  switch (a.dtype) {
+    case LUNARA_F16:
+      attn_simt_kernel<__half><<<grid, 128, 0, stream>>>(static_cast<const __half*>(a.Q),
+                                                         static_cast<const __half*>(a.K),
+                                                         static_cast<const __half*>(a.V), static_cast<__half*>(a.O),
+                                                         a);
+      break;
+    case LUNARA_BF16:
+      attn_simt_kernel<__nv_bfloat16><<<grid, 128, 0, stream>>>(
+          static_cast<const __nv_bfloat16*>(a.Q), static_cast<const __nv_bfloat16*>(a.K),
+          static_cast<const __nv_bfloat16*>(a.V), static_cast<__nv_bfloat16*>(a.O), a);
+      break;
+    default:
+      attn_simt_kernel<float><<<grid, 128, 0, stream>>>(static_cast<const float*>(a.Q),
+                                                        static_cast<const float*>(a.K),
+                                                        static_cast<const float*>(a.V), static_cast<float*>(a.O), a);
+      break;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace lunara

@@ -1,0 +1,506 @@
+// GEMM with fused epilogue: C = act(A * B + bias) + residual.
+//
+// tcgen05 path (f16 / bf16, TMA-compatible strides):
+//   persistent, warp-specialised kernel, one CTA per SM, 192 threads
+//     warp 0      TMA producer: A [128 x 64] and B [BN x 64] tiles, 128-byte
+//                 swizzle, into a STAGES-deep shared-memory ring
+//     warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//                 (M=128, N=BN, K=16 per instruction, fp32 accumulate)
+//     warps 2..5  epilogue: tcgen05.ld of the accumulator (thread = row),
+//                 bias + activation + residual in fp32, one rounding, 16-byte
+//                 global stores
+//   Two TMEM accumulators (2 x BN fp32 columns) let the epilogue of tile i
+//   overlap the main loop of tile i+1. No TMA multicast is used anywhere (the
+//   same kernel runs in multi-GPU jobs).
+// SIMT path: any shape / stride / dtype (incl. f32), 64x64 register tiles.
+//
+// Semantics follow the reference GEMM template,
+// lunara/codegen/triton_emitter.py:107-152: fp32 accumulation over K, then
+// bias and activation (145-147). The reference rounds to the output dtype
+// before the bias/activation; here the epilogue stays in fp32 and rounds once.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <type_traits>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace lunara {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kEpiWarps = 4;
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in limit per block on sm_100
+
+struct EpiParams {
+  void* C;
+  const void* bias;
+  const void* residual;
+  int64_t ldc, ldr;
+  int M, N;
+  int act;
+  int vec_ok;  // C / residual / bias allow 16-byte accesses
+};
+
+__host__ __device__ constexpr int gemm_stages(int bn) {
+  return std::min(8, (kMaxDynSmem - 2048) / (BM * BK * 2 + bn * BK * 2));
+}
+
+__host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
+  return (2 * bn <= 128) ? 128u : (2 * bn <= 256 ? 256u : 512u);
+}
+
+constexpr int gemm_smem_bytes(int bn, int stages) { return stages * (BM * BK * 2 + bn * BK * 2) + 1024 + 256; }
+
+// Epilogue for 32 consecutive accumulator columns of one row.
+template <typename T>
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int row, int col0, const EpiParams& ep) {
+  if (row >= ep.M) return;
+  float f[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(acc[i]);
+  const bool full = (col0 + 32 <= ep.N) && ep.vec_ok;
+  if (ep.bias != nullptr) {
+    const T* b = static_cast<const T*>(ep.bias) + col0;
+    if (full) {
+      const uint4* bv = reinterpret_cast<const uint4*>(b);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 u = __ldg(bv + q);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float2 p = Io<T>::unpack2(w[h]);
+          f[q * 8 + 2 * h] += p.x;
+          f[q * 8 + 2 * h + 1] += p.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < ep.N) f[i] += Io<T>::to_f(b[i]);
+    }
+  }
+  if (ep.act != LUNARA_ACT_NONE) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) f[i] = apply_act(f[i], ep.act);
+  }
+  if (ep.residual != nullptr) {
+    const T* r = static_cast<const T*>(ep.residual) + static_cast<int64_t>(row) * ep.ldr + col0;
+    if (full) {
+      const uint4* rv = reinterpret_cast<const uint4*>(r);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 u = __ldg(rv + q);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float2 p = Io<T>::unpack2(w[h]);
+          f[q * 8 + 2 * h] += p.x;
+          f[q * 8 + 2 * h + 1] += p.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < ep.N) f[i] += Io<T>::to_f(r[i]);
+    }
+  }
+  T* c = static_cast<T*>(ep.C) + static_cast<int64_t>(row) * ep.ldc + col0;
+  if (full) {
+    uint4* cv = reinterpret_cast<uint4*>(c);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 u;
+      u.x = Io<T>::pack2(f[q * 8 + 0], f[q * 8 + 1]);
+      u.y = Io<T>::pack2(f[q * 8 + 2], f[q * 8 + 3]);
+      u.z = Io<T>::pack2(f[q * 8 + 4], f[q * 8 + 5]);
+      u.w = Io<T>::pack2(f[q * 8 + 6], f[q * 8 + 7]);
+      cv[q] = u;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col0 + i < ep.N) c[i] = Io<T>::from_f(f[i]);
+  }
+}
+
+template <typename T, int BN, bool B_KMAJOR>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                   const EpiParams ep, const int M, const int N, const int K, const int STAGES,
+                   unsigned int* err) {
+  // STAGES (ring depth) is chosen on the host, 2 <= STAGES <= gemm_stages(BN);
+  // the dynamic shared-memory size is sized for it.
+  constexpr uint32_t A_BYTES = BM * BK * 2;
+  constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr uint32_t TMEM_COLS = tmem_cols_for(BN);
+  constexpr uint32_t ACC_STRIDE = TMEM_COLS / 2;  // column offset of the second accumulator
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t IDESC = idesc_f16(BM, BN, kBF16, false, !B_KMAJOR);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m_tiles = (M + BM - 1) / BM;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int kblocks = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], kEpiWarps);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------ TMA producer --
+      tma_prefetch_desc(&tma_a);
+      tma_prefetch_desc(&tma_b);
+      uint32_t stage = 0, phase = 0, issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        const int m0 = (tile % m_tiles) * BM;
+        const int n0 = (tile / m_tiles) * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, err, kErrGemmProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[stage], A_BYTES + B_BYTES);
+          tma_load_2d(sA + stage * A_BYTES, &tma_a, &full_bar[stage], kb * BK, m0);
+          if constexpr (B_KMAJOR) {
+            tma_load_2d(sB + stage * B_BYTES, &tma_b, &full_bar[stage], kb * BK, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sB + stage * B_BYTES + j * (BK * 128), &tma_b, &full_bar[stage], n0 + j * 64, kb * BK);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let every load already issued land before the CTA can exit.
+        const uint32_t first = issued > STAGES ? issued - STAGES : 0u;
+        for (uint32_t i = first; i < issued; ++i)
+          mbar_drain_wait(&full_bar[i % STAGES], (i / STAGES) & 1u, 1000000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------- MMA issuer --
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, err, kErrGemmMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * ACC_STRIDE;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, err, kErrGemmMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = sw128_desc(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = B_KMAJOR ? sw128_desc(b_addr + k * 32, 16, 1024)
+                                         : sw128_desc(b_addr + k * 2048, BK * 128, 1024);
+            umma_f16_ss(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        // Wait for the MMAs already issued before TMEM is released.
+        umma_commit(drain_bar);
+        mbar_drain_wait(drain_bar, 0, 1000000000ull);
+      }
+    }
+  } else {
+    // ----------------------------------------------------------- epilogue --
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = quarter * 32 + lane;
+    uint32_t acc = 0, acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int m0 = (tile % m_tiles) * BM;
+      const int n0 = (tile / m_tiles) * BN;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, err, kErrGemmEpilogue)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * ACC_STRIDE;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(t_row + c, v);
+        tmem_ld_wait();
+        epilogue_chunk<T>(v, m0 + r, n0 + c, ep);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------ SIMT path ----
+constexpr int ST = 64;   // output tile
+constexpr int SK = 16;   // K step
+
+template <typename T>
+__global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A, const T* __restrict__ B,
+                                                        const EpiParams ep, int64_t K, int64_t lda, int64_t ldb,
+                                                        int b_layout) {
+  __shared__ float As[SK][ST + 1];
+  __shared__ float Bs[SK][ST + 1];
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * ST, n0 = static_cast<int64_t>(blockIdx.x) * ST;
+  float acc[4][4] = {};
+  for (int64_t k0 = 0; k0 < K; k0 += SK) {
+    for (int i = threadIdx.x; i < SK * ST; i += 256) {
+      const int kk = i % SK, mm = i / SK;
+      const int64_t gm = m0 + mm, gk = k0 + kk;
+      As[kk][mm] = (gm < ep.M && gk < K) ? Io<T>::to_f(A[gm * lda + gk]) : 0.f;
+      const int nn = i % ST, kb = i / ST;
+      const int64_t gn = n0 + nn, gk2 = k0 + kb;
+      float bval = 0.f;
+      if (gn < ep.N && gk2 < K)
+        bval = Io<T>::to_f(b_layout == LUNARA_B_KN ? B[gk2 * ldb + gn] : B[gn * ldb + gk2]);
+      Bs[kb][nn] = bval;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < SK; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  const T* bias = static_cast<const T*>(ep.bias);
+  const T* res = static_cast<const T*>(ep.residual);
+  T* C = static_cast<T*>(ep.C);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t gm = m0 + ty * 4 + i;
+    if (gm >= ep.M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t gn = n0 + tx * 4 + j;
+      if (gn >= ep.N) continue;
+      float v = acc[i][j];
+      if (bias) v += Io<T>::to_f(bias[gn]);
+      v = apply_act(v, ep.act);
+      if (res) v += Io<T>::to_f(res[gm * ep.ldr + gn]);
+      C[gm * ep.ldc + gn] = Io<T>::from_f(v);
+    }
+  }
+}
+
+// ------------------------------------------------------------ host side ----
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+EpiParams make_epi(const GemmArgs& g) {
+  EpiParams ep{};
+  ep.C = g.C;
+  ep.bias = g.bias;
+  ep.residual = g.residual;
+  ep.ldc = g.ldc;
+  ep.ldr = g.ldr;
+  ep.M = static_cast<int>(g.M);
+  ep.N = static_cast<int>(g.N);
+  ep.act = g.act;
+  ep.vec_ok = al16(g.C) && (g.ldc % 8 == 0) && (g.bias == nullptr || al16(g.bias)) &&
+              (g.residual == nullptr || (al16(g.residual) && g.ldr % 8 == 0));
+  return ep;
+}
+
+bool encode_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer, uint64_t stride_bytes,
+               uint32_t box_inner, uint32_t box_outer) {
+  auto encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(tensor_map_encoder());
+  if (encode == nullptr) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {stride_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      dtype == LUNARA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Estimated cost of one GEMM for a tile width: rounds of persistent tiles
+// times per-tile main-loop cycles (tensor-pipe bound 2*BN per 64-deep K block,
+// shared-memory-read bound 128+BN) plus a fixed per-tile overhead.
+double gemm_cost(int64_t M, int64_t N, int64_t K, int bn, int sms) {
+  const int64_t tiles = ceil_div64(M, BM) * ceil_div64(N, bn);
+  const int64_t rounds = ceil_div64(tiles, sms);
+  const double per_kb = std::max(2.0 * bn, 128.0 + bn);
+  return static_cast<double>(rounds) * (static_cast<double>(ceil_div64(K, BK)) * per_kb + 600.0);
+}
+
+int choose_block_n(int64_t M, int64_t N, int64_t K, int sms) {
+  static const int kChoices[] = {256, 192, 128, 64};
+  int best = 256;
+  double best_cost = 1e300;
+  for (int bn : kChoices) {
+    const double c = gemm_cost(M, N, K, bn, sms);
+    if (c < best_cost * 0.999) {
+      best_cost = c;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+template <typename T, int BN, bool B_KMAJOR>
+cudaError_t run_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, cudaStream_t s) {
+  auto kern = gemm_tc_kernel<T, BN, B_KMAJOR>;
+  constexpr int kMaxStages = gemm_stages(BN);
+  static_assert(gemm_smem_bytes(BN, kMaxStages) <= kMaxDynSmem, "shared memory budget");
+  const int stages = (g.stages >= 2 && g.stages <= kMaxStages) ? g.stages : kMaxStages;
+  const int smem = gemm_smem_bytes(BN, stages);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       gemm_smem_bytes(BN, kMaxStages));
+  if (e != cudaSuccess) return e;
+  const int sms = device_num_sms();
+  const int64_t tiles = ceil_div64(g.M, BM) * ceil_div64(g.N, BN);
+  int64_t grid = g.num_ctas > 0 ? g.num_ctas : sms;
+  if (grid > tiles) grid = tiles;
+  unsigned int* err = device_error_word();
+  if (err == nullptr) return cudaErrorInvalidDevice;
+  kern<<<static_cast<unsigned>(grid), kGemmThreads, smem, s>>>(ma, mb, make_epi(g), static_cast<int>(g.M),
+                                                               static_cast<int>(g.N), static_cast<int>(g.K),
+                                                               stages, err);
+  return cudaGetLastError();
+}
+
+template <typename T, bool B_KMAJOR>
+cudaError_t dispatch_bn(const GemmArgs& g, int bn, cudaStream_t s) {
+  CUtensorMap ma, mb;
+  if (!encode_2d(&ma, g.A, g.dtype, g.K, g.M, g.lda * 2, BK, BM)) return cudaErrorInvalidValue;
+  const bool ok_b = B_KMAJOR ? encode_2d(&mb, g.B, g.dtype, g.K, g.N, g.ldb * 2, BK, bn)
+                             : encode_2d(&mb, g.B, g.dtype, g.N, g.K, g.ldb * 2, 64, BK);
+  if (!ok_b) return cudaErrorInvalidValue;
+  switch (bn) {
+    case 64: return run_tc<T, 64, B_KMAJOR>(g, ma, mb, s);
+    case 128: return run_tc<T, 128, B_KMAJOR>(g, ma, mb, s);
+    case 192: return run_tc<T, 192, B_KMAJOR>(g, ma, mb, s);
+    default: return run_tc<T, 256, B_KMAJOR>(g, ma, mb, s);
+  }
+}
+
+}  // namespace
+
+bool gemm_tc_supported(const GemmArgs& g) {
+  if (g.dtype != LUNARA_F16 && g.dtype != LUNARA_BF16) return false;
+  if (g.M < 1 || g.N < 1 || g.K < 1) return false;
+  if (g.M >= (int64_t{1} << 31) || g.N >= (int64_t{1} << 31) || g.K >= (int64_t{1} << 31)) return false;
+  if (!al16(g.A) || !al16(g.B)) return false;
+  if (g.lda % 8 != 0 || g.ldb % 8 != 0) return false;
+  return true;
+}
+
+cudaError_t launch_gemm_tcgen05(const GemmArgs& g, cudaStream_t stream) {
+  int bn = g.block_n;
+  if (bn != 64 && bn != 128 && bn != 192 && bn != 256) bn = choose_block_n(g.M, g.N, g.K, device_num_sms());
+  const bool kmajor = g.b_layout == LUNARA_B_NK;
+  if (g.dtype == LUNARA_BF16)
+    return kmajor ? dispatch_bn<__nv_bfloat16, true>(g, bn, stream) : dispatch_bn<__nv_bfloat16, false>(g, bn, stream);
+  return kmajor ? dispatch_bn<__half, true>(g, bn, stream) : dispatch_bn<__half, false>(g, bn, stream);
+}
+
+cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t stream) {
+  if (g.M == 0 || g.N == 0) return cudaSuccess;
+  const dim3 grid(static_cast<unsigned>(ceil_div64(g.N, ST)), static_cast<unsigned>(ceil_div64(g.M, ST)));
+  const EpiParams ep = make_epi(g);
+  switch (g.dtype) {
+    case LUNARA_F16:
+      gemm_simt_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half*>(g.A),
+                                                         static_cast<const __half*>(g.B), ep, g.K, g.lda, g.ldb,
+                                                         g.b_layout);
+      break;
+    case LUNARA_BF16:
+      gemm_simt_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(g.A),
+                                                                static_cast<const __nv_bfloat16*>(g.B), ep, g.K,
+                                                                g.lda, g.ldb, g.b_layout);
+      break;
+    default:
+      gemm_simt_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(g.A),
+                                                        static_cast<const float*>(g.B), ep, g.K, g.lda, g.ldb,
+                                                        g.b_layout);
+      break;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace lunara

@@ -1,0 +1,74 @@
+// Internal launcher prototypes shared between the kernel translation units and
+// the C-ABI layer (abi.cu). Launchers validate nothing beyond what their
+// kernel needs; argument checking happens in abi.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace lunara {
+
+int device_num_sms();
+
+// Device address of the library's error word on the current device (cached
+// per device); nullptr when the symbol cannot be resolved.
+unsigned int* device_error_word();
+
+cudaError_t launch_layernorm(const void* X, const void* gamma, const void* beta, void* Y, int64_t M, int64_t N,
+                             float eps, int dtype, cudaStream_t stream);
+
+cudaError_t launch_softmax(const void* X, void* Y, int64_t M, int64_t N, int dtype, cudaStream_t stream);
+
+cudaError_t launch_eltwise_unary(int act, const void* X, void* Y, int64_t n, int dtype, cudaStream_t stream);
+cudaError_t launch_eltwise_binary(int op, const void* X, const void* Yin, void* Out, int64_t n, int dtype,
+                                  cudaStream_t stream);
+cudaError_t launch_bias_act(const void* X, const void* bias, void* Y, int64_t rows, int64_t cols, int act, int dtype,
+                            cudaStream_t stream);
+
+cudaError_t launch_gather(const void* src, const int64_t* index, void* dst, int64_t n_index, int64_t src_rows,
+                          int64_t row_bytes, cudaStream_t stream);
+cudaError_t launch_copy_strided(const void* src, void* dst, int ndim, const int64_t* sizes,
+                                const int64_t* src_strides, int64_t elem_bytes, cudaStream_t stream);
+
+struct GemmArgs {
+  const void* A;
+  const void* B;
+  void* C;
+  const void* bias;
+  const void* residual;
+  int64_t M, N, K;
+  int64_t lda, ldb, ldc, ldr;
+  int b_layout;  // lunara_b_layout
+  int dtype;     // lunara_dtype
+  int act;       // lunara_activation
+  int block_n;   // 0 = auto
+  int stages;    // 0 = auto
+  int num_ctas;  // 0 = auto
+};
+
+// True when the tcgen05/TMA path accepts the shapes, strides and pointers.
+bool gemm_tc_supported(const GemmArgs& g);
+cudaError_t launch_gemm_tcgen05(const GemmArgs& g, cudaStream_t stream);
+cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t stream);
+
+struct AttnArgs {
+  const void* Q;
+  const void* K;
+  const void* V;
+  void* O;
+  int64_t B, H, Sq, Skv, D;
+  int64_t qs[4], ks[4], vs[4], os[4];  // element strides (batch, head, seq, dim)
+  float scale;
+  int causal;
+  int dtype;
+};
+
+bool attention_tc_supported(const AttnArgs& a);
+cudaError_t launch_attention_tcgen05(const AttnArgs& a, cudaStream_t stream);
+cudaError_t launch_attention_simt(const AttnArgs& a, cudaStream_t stream);
+
+// Resolves cuTensorMapEncodeTiled through the runtime's driver entry point
+// (the library does not link libcuda directly). Returns nullptr on failure.
+void* tensor_map_encoder();
+
+}  // namespace lunara

@@ -1,0 +1,135 @@
+"""Per-kernel benchmark workloads (the non-block benchmark configurations).
+
+  gemm              C = A B, M=N=K=4096 fp16, plus the bias+GELU epilogue variant
+  attention         B2 H12 S2048 D64 fp16, non-causal   (25.77 GFLOP)
+  attention_causal  same, causal                          (12.88 GFLOP, half)
+  layernorm         16384 x 768 fp16                      (50.33 MB moved)
+  bias_gelu         16384 x 3072 fp16 + bias, tanh GELU   (201.33 MB moved)
+  stack             12-layer encoder stack, batch 64 split over the ranks
+
+Each step is one launch (or one stack forward) bracketed by CUDA events, with
+a 256 MB L2-flush write between steps outside the events. Used by bench.py.
+"""
+from __future__ import annotations
+
+import json
+import statistics
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def _time_steps(fn, steps, warmup, flush):
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        flush.zero_()
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        fn()
+        e.record(stream)
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    return times
+
+
+def run(workload, args, rank, world, device):
+    from oracle import inputs
+    from lunara_b200.runtime import ops
+    hbm, tflops_peak, src = _peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    line = {"steps": args.steps, "warmup": args.warmup, "n_gpus": world, "data": "synthetic (seeded)"}
+    if workload == "gemm":
+        a, b, bias = inputs.gemm_inputs()
+        a, b, bias = a.half().to(device), b.half().to(device), bias.half().to(device)
+        c = torch.empty(4096, 4096, dtype=torch.float16, device=device)
+        t_plain = _time_steps(lambda: ops.gemm(a, b, c), args.steps, args.warmup, flush)
+        t_fused = _time_steps(lambda: ops.gemm(a, b, c, bias=bias, activation="gelu_tanh"), args.steps,
+                              args.warmup, flush)
+        flops = 2.0 * 4096 ** 3
+        tp = flops / (statistics.median(t_plain) * 1e-3) / 1e12
+        tf = flops / (statistics.median(t_fused) * 1e-3) / 1e12
+        line.update(metric="GEMM 4096^3 fp16 TFLOP/s", value=tp, unit="TFLOP/s", dtype="f16",
+                    config={"workload": "GEMM M=N=K=4096 fp16 row-major, fp32 accumulate"},
+                    ms_per_step=statistics.median(t_plain), bias_gelu_tflops=tf,
+                    roofline={"bound": "tensor", "achieved": tp, "peak": tflops_peak, "unit": "TFLOP/s",
+                              "frac": tp / tflops_peak, "peak_source": f"{src} bf16 burst"})
+    elif workload in ("attention", "attention_causal"):
+        causal = workload == "attention_causal"
+        q, k, v = (t.half().to(device) for t in inputs.attention_inputs())
+        o = torch.empty_like(q)
+        t = _time_steps(lambda: ops.attention(q, k, v, causal=causal, out=o), args.steps, args.warmup, flush)
+        flops = 4.0 * 2 * 12 * 2048 * 2048 * 64 * (0.5 if causal else 1.0)
+        ach = flops / (statistics.median(t) * 1e-3) / 1e12
+        line.update(metric=f"attention B2 H12 S2048 D64 fp16 {'causal' if causal else 'non-causal'} TFLOP/s",
+                    value=ach, unit="TFLOP/s", dtype="f16", ms_per_step=statistics.median(t),
+                    config={"workload": "SDPA B2 H12 S2048 D64 fp16, scale 1/8",
+                            "flops_convention": "4*B*H*S^2*D, halved for causal"},
+                    roofline={"bound": "tensor", "achieved": ach, "peak": tflops_peak, "unit": "TFLOP/s",
+                              "frac": ach / tflops_peak, "peak_source": f"{src} bf16 burst"})
+    elif workload == "layernorm":
+        x, w, b = inputs.layernorm_inputs()
+        x, w, b = x.half().to(device), w.half().to(device), b.half().to(device)
+        y = torch.empty_like(x)
+        t = _time_steps(lambda: ops.layernorm(x, w, b, 1e-5, out=y), args.steps, args.warmup, flush)
+        nbytes = 2.0 * 16384 * 768 * 2 + 2 * 768 * 2
+        gbs = nbytes / (statistics.median(t) * 1e-3) / 1e9
+        line.update(metric="LayerNorm 16384x768 fp16 GB/s", value=gbs, unit="GB/s", dtype="f16",
+                    ms_per_step=statistics.median(t), config={"workload": "LayerNorm 16384x768 fp16"},
+                    roofline={"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                              "peak_source": f"{src} copy"})
+    elif workload == "bias_gelu":
+        x, bias = inputs.bias_gelu_inputs()
+        x, bias = x.half().to(device), bias.half().to(device)
+        y = torch.empty_like(x)
+        t = _time_steps(lambda: ops.bias_act(x, bias, "gelu_tanh", out=y), args.steps, args.warmup, flush)
+        nbytes = 2.0 * 16384 * 3072 * 2 + 3072 * 2
+        gbs = nbytes / (statistics.median(t) * 1e-3) / 1e9
+        line.update(metric="bias+GELU 16384x3072 fp16 GB/s", value=gbs, unit="GB/s", dtype="f16",
+                    ms_per_step=statistics.median(t), config={"workload": "bias + tanh-GELU 16384x3072 fp16"},
+                    roofline={"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                              "peak_source": f"{src} copy"})
+    elif workload == "stack":
+        from lunara_b200.runtime.encoder import EncoderStack, GraphRunner
+        per_rank = 64 // world
+        x, ws = inputs.stack_inputs(batch=64, seq=512, layers=12, seed=4)
+        xs = x[rank * per_rank:(rank + 1) * per_rank]
+        st = EncoderStack(ws, batch=per_rank, seq=512, num_heads=12, device=device)
+        st.x.copy_(xs.half().reshape(-1, 768).to(device))
+        runner = GraphRunner(st.run_kernels)
+        t = _time_steps(runner.replay, args.steps, args.warmup, flush)
+        total = sum(t)
+        if world > 1:
+            import torch.distributed as dist
+            tt = torch.tensor([total], dtype=torch.float64, device=device)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            total = float(tt.item())
+        runner.release()
+        tokens = 64 * 512 * args.steps
+        val = tokens / (total * 1e-3)
+        flops = 12 * 8 * 64.42e9 * args.steps
+        ach = flops / (total * 1e-3) / 1e12
+        line.update(metric="12-layer encoder stack tokens/s (B64,S512,H768)", value=val, unit="tokens/s",
+                    dtype="f16", scaling="strong", ms_per_step=total / args.steps,
+                    config={"workload": "12-layer encoder stack B64 S512 fp16", "global_batch": 64,
+                            "per_rank_batch": per_rank, "parallelism": f"batch-sharded x{world}"},
+                    roofline={"bound": "tensor", "achieved": ach, "peak": tflops_peak * world,
+                              "unit": "TFLOP/s", "frac": ach / (tflops_peak * world),
+                              "peak_source": f"{src} bf16 burst x {world} GPUs"})
+    else:
+        raise ValueError(workload)
+    return line
