@@ -256,7 +256,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int c = 0; c < kKvBlock / 32; ++c) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(tS + c * 32, v);
-        tmem_ld_wait();
+        tmem_ld_wait_regs(v);
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           float s = __uint_as_float(v[i]);
@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int c = 0; c < kHeadDim / 32; ++c) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(tO + c * 32, v);
-          tmem_ld_wait();
+          tmem_ld_wait_regs(v);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha_pend, __uint_as_float(v[i]));
         }
@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int c = 0; c < kKvBlock / 32; ++c) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(tS + c * 32, v);
-        tmem_ld_wait();
+        tmem_ld_wait_regs(v);
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int c = 0; c < kHeadDim / 32; ++c) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(tO + c * 32, v);
-          tmem_ld_wait();
+          tmem_ld_wait_regs(v);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha_pend, __uint_as_float(v[i]));
         }

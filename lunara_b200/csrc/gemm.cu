@@ -1,14 +1,16 @@
 // GEMM with fused epilogue: C = act(A * B + bias) + residual.
 //
 // tcgen05 path (f16 / bf16, TMA-compatible strides):
-//   persistent, warp-specialised kernel, one CTA per SM, 192 threads
+//   persistent, warp-specialised kernel, one CTA per SM, 320 threads
 //     warp 0      TMA producer: A [128 x 64] and B [BN x 64] tiles, 128-byte
 //                 swizzle, into a STAGES-deep shared-memory ring
 //     warp 1      TMEM allocator + single-thread tcgen05.mma issuer
 //                 (M=128, N=BN, K=16 per instruction, fp32 accumulate)
-//     warps 2..5  epilogue: tcgen05.ld of the accumulator (thread = row),
-//                 bias + activation + residual in fp32, one rounding, 16-byte
-//                 global stores
+//     warps 2..9  epilogue (two warps per TMEM lane quarter, half the columns
+//                 each): tcgen05.ld of the accumulator one 32-column chunk
+//                 ahead (thread = row), bias (staged per warp in shared
+//                 memory) + activation + residual (loaded one chunk ahead) in
+//                 fp32, one rounding, 16-byte global stores
 //   Two TMEM accumulators (2 x BN fp32 columns) let the epilogue of tile i
 //   overlap the main loop of tile i+1. No TMA multicast is used anywhere (the
 //   same kernel runs in multi-GPU jobs).
@@ -31,9 +33,11 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kEpiWarps = 4;
-constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+constexpr int kEpiWarps = 8;        // two warps per TMEM lane quarter, each owning half the tile's columns
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kGemmThreads = 64 + kEpiThreads;
 constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in limit per block on sm_100
+constexpr int kSmemReserve = 6144;   // barriers, bias staging (8 warps x 128 fp32), 1 KB alignment slack
 
 struct EpiParams {
   void* C;
@@ -46,56 +50,73 @@ struct EpiParams {
 };
 
 __host__ __device__ constexpr int gemm_stages(int bn) {
-  return std::min(8, (kMaxDynSmem - 2048) / (BM * BK * 2 + bn * BK * 2));
+  return std::min(8, (kMaxDynSmem - kSmemReserve) / (BM * BK * 2 + bn * BK * 2));
 }
 
 __host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
   return (2 * bn <= 128) ? 128u : (2 * bn <= 256 ? 256u : 512u);
 }
 
-constexpr int gemm_smem_bytes(int bn, int stages) { return stages * (BM * BK * 2 + bn * BK * 2) + 1024 + 256; }
+constexpr int gemm_smem_bytes(int bn, int stages) {
+  return stages * (BM * BK * 2 + bn * BK * 2) + kSmemReserve;
+}
 
-// Epilogue for 32 consecutive accumulator columns of one row.
+// Activation over a 32-value chunk; the switch is taken once per chunk.
+__device__ __forceinline__ void act_chunk(float (&f)[32], int act) {
+  switch (act) {
+    case LUNARA_ACT_NONE:
+      break;
+#define LUNARA_ACT_CASE(CODE)                                          \
+  case CODE:                                                           \
+    _Pragma("unroll") for (int i = 0; i < 32; ++i) f[i] = apply_act(f[i], CODE); \
+    break;
+      LUNARA_ACT_CASE(LUNARA_ACT_RELU)
+      LUNARA_ACT_CASE(LUNARA_ACT_GELU_ERF)
+      LUNARA_ACT_CASE(LUNARA_ACT_GELU_TANH)
+      LUNARA_ACT_CASE(LUNARA_ACT_SIGMOID)
+      LUNARA_ACT_CASE(LUNARA_ACT_TANH)
+#undef LUNARA_ACT_CASE
+    default:
+      break;
+  }
+}
+
+// Residual values of one chunk, loaded one chunk ahead of their use.
+struct ResChunk {
+  uint4 q[4];
+};
+
 template <typename T>
-__device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int row, int col0, const EpiParams& ep) {
+__device__ __forceinline__ void load_residual(ResChunk& rc, int row, int col0, const EpiParams& ep) {
+  if (ep.residual == nullptr || row >= ep.M) return;
+  const T* r = static_cast<const T*>(ep.residual) + static_cast<int64_t>(row) * ep.ldr + col0;
+  if ((col0 + 32 <= ep.N) && ep.vec_ok) {
+    const uint4* rv = reinterpret_cast<const uint4*>(r);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) rc.q[q] = __ldg(rv + q);
+  }
+}
+
+// Epilogue for 32 consecutive accumulator columns of one row: + bias (staged
+// in shared memory as fp32), activation, + residual, one rounding, store.
+template <typename T>
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int row, int col0, const float* s_bias,
+                                               const ResChunk& rc, const EpiParams& ep) {
   if (row >= ep.M) return;
   float f[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(acc[i]);
   const bool full = (col0 + 32 <= ep.N) && ep.vec_ok;
   if (ep.bias != nullptr) {
-    const T* b = static_cast<const T*>(ep.bias) + col0;
-    if (full) {
-      const uint4* bv = reinterpret_cast<const uint4*>(b);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint4 u = __ldg(bv + q);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const float2 p = Io<T>::unpack2(w[h]);
-          f[q * 8 + 2 * h] += p.x;
-          f[q * 8 + 2 * h + 1] += p.y;
-        }
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (col0 + i < ep.N) f[i] += Io<T>::to_f(b[i]);
-    }
+    for (int i = 0; i < 32; ++i) f[i] += s_bias[i];
   }
-  if (ep.act != LUNARA_ACT_NONE) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) f[i] = apply_act(f[i], ep.act);
-  }
+  act_chunk(f, ep.act);
   if (ep.residual != nullptr) {
-    const T* r = static_cast<const T*>(ep.residual) + static_cast<int64_t>(row) * ep.ldr + col0;
     if (full) {
-      const uint4* rv = reinterpret_cast<const uint4*>(r);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const uint4 u = __ldg(rv + q);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+        const uint32_t w[4] = {rc.q[q].x, rc.q[q].y, rc.q[q].z, rc.q[q].w};
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
           const float2 p = Io<T>::unpack2(w[h]);
@@ -104,6 +125,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int ro
         }
       }
     } else {
+      const T* r = static_cast<const T*>(ep.residual) + static_cast<int64_t>(row) * ep.ldr + col0;
 #pragma unroll
       for (int i = 0; i < 32; ++i)
         if (col0 + i < ep.N) f[i] += Io<T>::to_f(r[i]);
@@ -153,6 +175,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* drain_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_bias = reinterpret_cast<float*>(drain_bar + 2);  // [8 epilogue warps][128] fp32
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -269,21 +292,48 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ----------------------------------------------------------- epilogue --
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    // Warps 2..9: warp & 3 is the TMEM lane quarter it may read (rows
+    // 32*q .. 32*q+31 of the tile); warps 2-5 take the first half of the
+    // tile's columns, warps 6-9 the second half.
+    constexpr int kHalf = BN / 2;
+    constexpr int kChunks = kHalf / 32;
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     uint32_t acc = 0, acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int m0 = (tile % m_tiles) * BM;
       const int n0 = (tile / m_tiles) * BN;
+      const int row = m0 + r;
+      const int c0 = n0 + half * kHalf;
+      // Stage this warp's slice of the bias in its own shared-memory region
+      // (fp32) while the MMAs run; only this warp reads it, so __syncwarp
+      // orders the writes before the reads and the previous tile's reads
+      // before these writes.
+      float* sb = s_bias + (warp - 2) * 128;
+      if (ep.bias != nullptr) {
+        for (int i = lane; i < kHalf; i += 32) {
+          const int col = c0 + i;
+          sb[i] = col < N ? Io<T>::to_f(static_cast<const T*>(ep.bias)[col]) : 0.f;
+        }
+      }
+      ResChunk res[2];
+      load_residual<T>(res[0], row, c0, ep);
+      __syncwarp();
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, err, kErrGemmEpilogue)) break;
       tc_fence_after();
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * ACC_STRIDE;
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(t_row + c, v);
-        tmem_ld_wait();
-        epilogue_chunk<T>(v, m0 + r, n0 + c, ep);
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * ACC_STRIDE +
+                             half * kHalf;
+      uint32_t v[2][32];
+      tmem_ld_32x32b_x32(t_row, v[0]);
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        tmem_ld_wait_regs(v[c & 1]);
+        if (c + 1 < kChunks) {
+          tmem_ld_32x32b_x32(t_row + (c + 1) * 32, v[(c + 1) & 1]);
+          load_residual<T>(res[(c + 1) & 1], row, c0 + (c + 1) * 32, ep);
+        }
+        epilogue_chunk<T>(v[c & 1], row, c0 + c * 32, sb + c * 32, res[c & 1], ep);
       }
       tc_fence_before();
       __syncwarp();
