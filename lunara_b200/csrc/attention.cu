@@ -38,7 +38,15 @@ constexpr int kQTile = 128;     // query rows per softmax warpgroup
 constexpr int kKvBlock = 128;   // keys per iteration
 constexpr int kHeadDim = 64;
 constexpr int kKvStages = 3;
-constexpr int kAttnThreads = 320;
+constexpr int kAttnThreads = 384;  // warpgroups: 0-1 softmax, 2 = TMA warp, MMA warp, 2 idle warps
+// Register split with setmaxnreg: the kernel launches with 168 registers per
+// thread (384 x 168 = 64512); warpgroup 2 drops to 56 and the two softmax
+// warpgroups rise to 224: 128 x 56 + 256 x 224 = 64512, exactly the launch total.
+constexpr int kLaunchRegs = 168;
+constexpr int kProducerRegs = 56;
+constexpr int kSoftmaxRegs = 224;
+static_assert(128 * kProducerRegs + 256 * kSoftmaxRegs <= kAttnThreads * kLaunchRegs, "register split");
+constexpr float kRescaleLog2 = 8.0f;
 constexpr uint32_t kTileBytes = 128 * 128;  // one [128 x 64] 16-bit tile
 constexpr int kAttnSmem = 2 * kTileBytes + 2 * kKvStages * kTileBytes + 2 * 2 * kTileBytes + 256 + 1024;
 constexpr uint32_t kAttnTmemCols = 512;
@@ -122,8 +130,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-
+  // Each role adjusts its register budget at the top of its own branch, so the
+  // compiler allocates every branch with that branch's budget.
   if (warp == 8) {
+    reg_dealloc<kProducerRegs>();
     if (lane == 0) {
       // -------------------------------------------------------- TMA producer --
       tma_prefetch_desc(&tq);
@@ -155,6 +165,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
     }
   } else if (warp == 9) {
+    reg_dealloc<kProducerRegs>();
     if (lane == 0) {
       // ---------------------------------------------------------- MMA issuer --
       bool ok = mbar_wait(q_full, 0, abort_flag, err, kErrAttnMma);
@@ -170,14 +181,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             umma_f16_ss(tmem_base + w * 128, sw128_desc(q_addr + k * 32, 16, 1024),
                         sw128_desc(k_addr + k * 32, 16, 1024), IDESC_S, k > 0 ? 1u : 0u);
         };
-        auto issue_pv = [&](int w, int st) {
+        auto issue_pv = [&](int w, int st, int j) {
           const uint32_t p_addr = p_base + w * 2 * kTileBytes;
           const uint32_t v_addr = smem_u32(sV + st * kTileBytes);
 #pragma unroll
           for (int k = 0; k < kKvBlock / 16; ++k)
             umma_f16_ss(tmem_base + 256 + w * 128,
                         sw128_desc(p_addr + (k / 4) * kTileBytes + (k % 4) * 32, 16, 1024),
-                        sw128_desc(v_addr + k * 2048, kTileBytes, 1024), IDESC_PV, k > 0 ? 1u : 0u);
+                        sw128_desc(v_addr + k * 2048, kTileBytes, 1024), IDESC_PV, (j > 0 || k > 0) ? 1u : 0u);
         };
         ok = mbar_wait(&k_full[0], 0, abort_flag, err, kErrAttnMma);
         if (ok) {
@@ -206,7 +217,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               break;
             }
             tc_fence_after();
-            issue_pv(w, st);
+            issue_pv(w, st, j);
             umma_commit(&o_full[w]);
             if (j + 1 < nbw) {
               issue_s(w, st1);
@@ -223,8 +234,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mbar_drain_wait(drain_bar, 0, 1000000000ull);
       }
     }
+  } else if (warp >= 10) {
+    reg_dealloc<kProducerRegs>();   // idle warps of warpgroup 2
   } else {
+    reg_alloc<kSoftmaxRegs>();
     // ------------------------------------------------------------- softmax --
+    // Thread = one query row. O accumulates in TMEM (the PV MMA adds onto it);
+    // the running maximum is only raised when a row's maximum grows by more
+    // than 2^kRescaleLog2, and O is rescaled in TMEM only then (P values up to
+    // 2^kRescaleLog2 are exact enough in fp16/bf16 and the sum is fp32).
     const int w = warp >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
@@ -236,10 +254,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t tO = tmem_base + lane_off + 256 + w * 128;
     uint8_t* myP = sP + w * 2 * kTileBytes;
     const float sl2 = p.scale_log2;
-    float m = -INFINITY, l = 0.f, alpha_pend = 0.f;
-    float o[kHeadDim];
-#pragma unroll
-    for (int i = 0; i < kHeadDim; ++i) o[i] = 0.f;
+    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
 
     for (int j = 0; j < my_nb; ++j) {
@@ -248,62 +263,68 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         break;
       }
       tc_fence_after();
+      // The whole 128-column score row: four TMEM loads, one wait.
+      uint32_t sc[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tS + c * 32, sc[c]);
+      tmem_ld_wait_regs(sc[0]);
+      reg_fence(sc[1]);
+      reg_fence(sc[2]);
+      reg_fence(sc[3]);
       const int kv0 = j * kKvBlock;
-      const bool need_mask = (kv0 + kKvBlock > p.Skv) || (p.causal && kv0 + kKvBlock - 1 > q_first);
-      // Pass 1: row maximum of the scores.
+      if ((kv0 + kKvBlock > p.Skv) || (p.causal && kv0 + kKvBlock - 1 > q_first)) {
+        // Keep key columns < Skv and (causal) <= this query row.
+        int lim = p.Skv - kv0;
+        if (p.causal && qrow - kv0 + 1 < lim) lim = qrow - kv0 + 1;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i >= lim) sc[c][i] = __float_as_uint(-INFINITY);
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < kKvBlock / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tS + c * 32, v);
-        tmem_ld_wait_regs(v);
+      for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float s = __uint_as_float(v[i]);
-          if (need_mask) {
-            const int col = kv0 + c * 32 + i;
-            if (col >= p.Skv || (p.causal && col > qrow)) s = -INFINITY;
-          }
-          mx = fmaxf(mx, s);
-        }
-      }
-      const float m_new = fmaxf(m, mx * sl2);
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = ex2_approx(m - m_use);
-      // The previous P V product must be done before P is overwritten; fold it in.
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sc[c][i]));
+      const float m_cand = mx * sl2;
+      // P of the previous block must have been consumed (and O updated) before
+      // P is overwritten and O is touched.
       if (j > 0) {
         if (!mbar_wait(&o_full[w], static_cast<uint32_t>(j - 1) & 1u, abort_flag, err, kErrAttnSoftmax)) {
           ok = false;
           break;
         }
         tc_fence_after();
+      }
+      if (j == 0) {
+        m_used = m_cand;
+      } else if (__any_sync(0xffffffffu, m_cand > m_used + kRescaleLog2)) {
+        const float m_next = fmaxf(m_used, m_cand);
+        const float alpha = ex2_approx(m_used - m_next);
+        l *= alpha;
+        m_used = m_next;
 #pragma unroll
         for (int c = 0; c < kHeadDim / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tO + c * 32, v);
-          tmem_ld_wait_regs(v);
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(tO + c * 32, ov);
+          tmem_ld_wait_regs(ov);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha_pend, __uint_as_float(v[i]));
+          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+          tmem_st_32x32b_x32(tO + c * 32, ov);
         }
+        tmem_st_wait();
       }
-      // Pass 2: P = exp2(S * scale * log2e - m), row sum, P -> swizzled smem.
+      const float m_off = (m_used == -INFINITY) ? 0.f : m_used;
+      // P = exp2(S * scale * log2e - m), row sum, P -> swizzled K-major smem tile.
       float sum = 0.f;
 #pragma unroll
-      for (int c = 0; c < kKvBlock / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tS + c * 32, v);
-        tmem_ld_wait_regs(v);
+      for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          float s0 = __uint_as_float(v[i]), s1 = __uint_as_float(v[i + 1]);
-          if (need_mask) {
-            const int col = kv0 + c * 32 + i;
-            if (col >= p.Skv || (p.causal && col > qrow)) s0 = -INFINITY;
-            if (col + 1 >= p.Skv || (p.causal && col + 1 > qrow)) s1 = -INFINITY;
-          }
-          const float e0 = ex2_approx(fmaf(s0, sl2, -m_use));
-          const float e1 = ex2_approx(fmaf(s1, sl2, -m_use));
+          const float e0 = ex2_approx(fmaf(__uint_as_float(sc[c][i]), sl2, -m_off));
+          const float e1 = ex2_approx(fmaf(__uint_as_float(sc[c][i + 1]), sl2, -m_off));
           sum += e0 + e1;
           pk[i / 2] = Io<T>::pack2(e0, e1);
         }
@@ -315,9 +336,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
       }
-      l = fmaf(l, alpha, sum);
-      m = m_new;
-      alpha_pend = alpha;
+      l += sum;
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_ready[w]);
@@ -325,26 +344,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (ok && my_nb > 0) {
       if (mbar_wait(&o_full[w], static_cast<uint32_t>(my_nb - 1) & 1u, abort_flag, err, kErrAttnSoftmax)) {
         tc_fence_after();
+        const float inv_l = 1.0f / l;
+        T* out = static_cast<T*>(p.O) + b * p.os_b + h * p.os_h + static_cast<int64_t>(qrow) * p.os_s;
+        uint4* ov4 = reinterpret_cast<uint4*>(out);
 #pragma unroll
         for (int c = 0; c < kHeadDim / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tO + c * 32, v);
-          tmem_ld_wait_regs(v);
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(tO + c * 32, ov);
+          tmem_ld_wait_regs(ov);
+          if (qrow < p.Sq) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha_pend, __uint_as_float(v[i]));
-        }
-        if (qrow < p.Sq) {
-          const float inv_l = 1.0f / l;
-          T* out = static_cast<T*>(p.O) + b * p.os_b + h * p.os_h + static_cast<int64_t>(qrow) * p.os_s;
-          uint4* ov = reinterpret_cast<uint4*>(out);
-#pragma unroll
-          for (int q = 0; q < kHeadDim / 8; ++q) {
-            uint4 u;
-            u.x = Io<T>::pack2(o[8 * q + 0] * inv_l, o[8 * q + 1] * inv_l);
-            u.y = Io<T>::pack2(o[8 * q + 2] * inv_l, o[8 * q + 3] * inv_l);
-            u.z = Io<T>::pack2(o[8 * q + 4] * inv_l, o[8 * q + 5] * inv_l);
-            u.w = Io<T>::pack2(o[8 * q + 6] * inv_l, o[8 * q + 7] * inv_l);
-            ov[q] = u;
+            for (int q = 0; q < 4; ++q) {
+              uint4 u;
+              u.x = Io<T>::pack2(__uint_as_float(ov[8 * q + 0]) * inv_l, __uint_as_float(ov[8 * q + 1]) * inv_l);
+              u.y = Io<T>::pack2(__uint_as_float(ov[8 * q + 2]) * inv_l, __uint_as_float(ov[8 * q + 3]) * inv_l);
+              u.z = Io<T>::pack2(__uint_as_float(ov[8 * q + 4]) * inv_l, __uint_as_float(ov[8 * q + 5]) * inv_l);
+              u.w = Io<T>::pack2(__uint_as_float(ov[8 * q + 6]) * inv_l, __uint_as_float(ov[8 * q + 7]) * inv_l);
+              ov4[c * 4 + q] = u;
+            }
           }
         }
       }
@@ -445,7 +462,13 @@ cudaError_t run_tc(const AttnArgs& a, cudaStream_t s) {
       !encode_4d(&mv, a.V, a.dtype, a.Skv, a.H, a.B, a.vs))
     return cudaErrorInvalidValue;
   auto kern = attn_tc_kernel<T>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+  // The setmaxnreg split assumes the kernel launches with exactly kLaunchRegs
+  // registers per thread; refuse to launch a build where that does not hold.
+  cudaFuncAttributes fa{};
+  cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+  if (e != cudaSuccess) return e;
+  if (fa.numRegs != kLaunchRegs) return cudaErrorInvalidConfiguration;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
   if (e != cudaSuccess) return e;
   AttnParams p{};
   p.O = a.O;

@@ -61,8 +61,16 @@ constexpr int gemm_smem_bytes(int bn, int stages) {
   return stages * (BM * BK * 2 + bn * BK * 2) + kSmemReserve;
 }
 
+// Epilogue modes (a template parameter, so the common cases carry no switch
+// and the epilogue code stays small enough for the instruction cache).
+enum EpiMode : int { kEpiPlain = 0, kEpiGeluTanh = 1, kEpiAnyAct = 2 };
+
+inline int epi_mode_for(int act) {
+  return act == LUNARA_ACT_NONE ? kEpiPlain : (act == LUNARA_ACT_GELU_TANH ? kEpiGeluTanh : kEpiAnyAct);
+}
+
 // Activation over a 32-value chunk; the switch is taken once per chunk.
-__device__ __forceinline__ void act_chunk(float (&f)[32], int act) {
+__device__ __noinline__ void act_chunk_any(float (&f)[32], int act) {
   switch (act) {
     case LUNARA_ACT_NONE:
       break;
@@ -99,7 +107,7 @@ __device__ __forceinline__ void load_residual(ResChunk& rc, int row, int col0, c
 
 // Epilogue for 32 consecutive accumulator columns of one row: + bias (staged
 // in shared memory as fp32), activation, + residual, one rounding, store.
-template <typename T>
+template <typename T, int EPI>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int row, int col0, const float* s_bias,
                                                const ResChunk& rc, const EpiParams& ep) {
   if (row >= ep.M) return;
@@ -111,7 +119,12 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int ro
 #pragma unroll
     for (int i = 0; i < 32; ++i) f[i] += s_bias[i];
   }
-  act_chunk(f, ep.act);
+  if constexpr (EPI == kEpiGeluTanh) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) f[i] = apply_act(f[i], LUNARA_ACT_GELU_TANH);
+  } else if constexpr (EPI == kEpiAnyAct) {
+    act_chunk_any(f, ep.act);
+  }
   if (ep.residual != nullptr) {
     if (full) {
 #pragma unroll
@@ -150,7 +163,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int ro
   }
 }
 
-template <typename T, int BN, bool B_KMAJOR>
+template <typename T, int BN, bool B_KMAJOR, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                    const EpiParams ep, const int M, const int N, const int K, const int STAGES,
@@ -324,16 +337,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * ACC_STRIDE +
                              half * kHalf;
+      // Chunks are processed in pairs (two register buffers, compile-time
+      // indices); the loop itself is not unrolled to keep the code small.
       uint32_t v[2][32];
       tmem_ld_32x32b_x32(t_row, v[0]);
-#pragma unroll
-      for (int c = 0; c < kChunks; ++c) {
-        tmem_ld_wait_regs(v[c & 1]);
+#pragma unroll 1
+      for (int c = 0; c < kChunks; c += 2) {
+        tmem_ld_wait_regs(v[0]);
         if (c + 1 < kChunks) {
-          tmem_ld_32x32b_x32(t_row + (c + 1) * 32, v[(c + 1) & 1]);
-          load_residual<T>(res[(c + 1) & 1], row, c0 + (c + 1) * 32, ep);
+          tmem_ld_32x32b_x32(t_row + (c + 1) * 32, v[1]);
+          load_residual<T>(res[1], row, c0 + (c + 1) * 32, ep);
         }
-        epilogue_chunk<T>(v[c & 1], row, c0 + c * 32, sb + c * 32, res[c & 1], ep);
+        epilogue_chunk<T, EPI>(v[0], row, c0 + c * 32, sb + c * 32, res[0], ep);
+        if (c + 1 < kChunks) {
+          tmem_ld_wait_regs(v[1]);
+          if (c + 2 < kChunks) {
+            tmem_ld_32x32b_x32(t_row + (c + 2) * 32, v[0]);
+            load_residual<T>(res[0], row, c0 + (c + 2) * 32, ep);
+          }
+          epilogue_chunk<T, EPI>(v[1], row, c0 + (c + 1) * 32, sb + (c + 1) * 32, res[1], ep);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -472,9 +495,9 @@ int choose_block_n(int64_t M, int64_t N, int64_t K, int sms) {
   return best;
 }
 
-template <typename T, int BN, bool B_KMAJOR>
+template <typename T, int BN, bool B_KMAJOR, int EPI>
 cudaError_t run_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, cudaStream_t s) {
-  auto kern = gemm_tc_kernel<T, BN, B_KMAJOR>;
+  auto kern = gemm_tc_kernel<T, BN, B_KMAJOR, EPI>;
   constexpr int kMaxStages = gemm_stages(BN);
   static_assert(gemm_smem_bytes(BN, kMaxStages) <= kMaxDynSmem, "shared memory budget");
   const int stages = (g.stages >= 2 && g.stages <= kMaxStages) ? g.stages : kMaxStages;
@@ -494,6 +517,16 @@ cudaError_t run_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& 
   return cudaGetLastError();
 }
 
+template <typename T, bool B_KMAJOR, int EPI>
+cudaError_t dispatch_epi(const GemmArgs& g, int bn, const CUtensorMap& ma, const CUtensorMap& mb, cudaStream_t s) {
+  switch (bn) {
+    case 64: return run_tc<T, 64, B_KMAJOR, EPI>(g, ma, mb, s);
+    case 128: return run_tc<T, 128, B_KMAJOR, EPI>(g, ma, mb, s);
+    case 192: return run_tc<T, 192, B_KMAJOR, EPI>(g, ma, mb, s);
+    default: return run_tc<T, 256, B_KMAJOR, EPI>(g, ma, mb, s);
+  }
+}
+
 template <typename T, bool B_KMAJOR>
 cudaError_t dispatch_bn(const GemmArgs& g, int bn, cudaStream_t s) {
   CUtensorMap ma, mb;
@@ -501,11 +534,10 @@ cudaError_t dispatch_bn(const GemmArgs& g, int bn, cudaStream_t s) {
   const bool ok_b = B_KMAJOR ? encode_2d(&mb, g.B, g.dtype, g.K, g.N, g.ldb * 2, BK, bn)
                              : encode_2d(&mb, g.B, g.dtype, g.N, g.K, g.ldb * 2, 64, BK);
   if (!ok_b) return cudaErrorInvalidValue;
-  switch (bn) {
-    case 64: return run_tc<T, 64, B_KMAJOR>(g, ma, mb, s);
-    case 128: return run_tc<T, 128, B_KMAJOR>(g, ma, mb, s);
-    case 192: return run_tc<T, 192, B_KMAJOR>(g, ma, mb, s);
-    default: return run_tc<T, 256, B_KMAJOR>(g, ma, mb, s);
+  switch (epi_mode_for(g.act)) {
+    case kEpiPlain: return dispatch_epi<T, B_KMAJOR, kEpiPlain>(g, bn, ma, mb, s);
+    case kEpiGeluTanh: return dispatch_epi<T, B_KMAJOR, kEpiGeluTanh>(g, bn, ma, mb, s);
+    default: return dispatch_epi<T, B_KMAJOR, kEpiAnyAct>(g, bn, ma, mb, s);
   }
 }
 
