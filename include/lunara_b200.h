@@ -65,14 +65,17 @@ typedef enum lunara_b_layout {
 
 /* Optional tile request for the GEMM (the sm_100a counterpart of TileConfig,
  * triton_emitter.py:44-56). Zero fields mean "choose automatically".
- *   block_n : 64, 128 or 256 (the tcgen05 MMA N of one 128-row tile)
+ *   block_n : tcgen05 MMA N: 64, 128, 192 or 256 for 128-row tiles of one
+ *             CTA; 128 or 256 for 256-row tiles of a CTA pair
  *   stages  : shared-memory pipeline depth (2..8)
- *   num_ctas: persistent grid size (0 = one CTA per SM) */
+ *   num_ctas: persistent grid size (0 = every SM / SM pair)
+ *   cta_pair: 1 = single-CTA tiles, 2 = CTA-pair tiles (cta_group::2),
+ *             0 = choose from the problem shape */
 typedef struct lunara_gemm_config {
   int32_t block_n;
   int32_t stages;
   int32_t num_ctas;
-  int32_t reserved;
+  int32_t cta_pair;
 } lunara_gemm_config;
 
 /* GEMM: C[M,N] = act(A[M,K] * B + bias[N]) + residual[M,N]

@@ -161,6 +161,7 @@ int lunara_gemm(const void* A, const void* B, void* C, const void* bias, const v
     g.block_n = config->block_n;
     g.stages = config->stages;
     g.num_ctas = config->num_ctas;
+    g.cta_pair = config->cta_pair;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (gemm_tc_supported(g)) return from_cuda(launch_gemm_tcgen05(g, s), "lunara_gemm(tcgen05)");

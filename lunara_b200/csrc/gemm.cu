@@ -377,6 +377,242 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ------------------------------------------------ CTA-pair (2-SM) tcgen05 ----
+// Same roles as gemm_tc_kernel, on a cluster of two CTAs that computes
+// 256 x BN output tiles with cta_group::2 MMAs (M=256, N=BN, K=16):
+//   * each CTA's TMA warp loads its own 128 rows of A and its own BN/2 rows
+//     (K-major) or columns (MN-major) of B -- no multicast -- and completes the
+//     bytes on the even CTA's full barrier, which the even CTA's producer armed
+//     with the pair's total;
+//   * the even CTA's MMA thread issues the pair's MMAs and commits (multicast
+//     to both CTAs) the smem-stage "empty" and the accumulator "full" barriers;
+//   * each CTA's epilogue reads its 128 accumulator rows from its own TMEM and
+//     arrives on the even CTA's accumulator "empty" barrier.
+// Per CTA and K block this moves 16 KB of A + BN/2 x 128 B of B for half of a
+// 256 x BN x 64 MMA: BN=256 halves the B traffic of the 1-CTA 128x256 tile.
+__host__ __device__ constexpr int pair_stages(int bn) {
+  return std::min(8, (kMaxDynSmem - kSmemReserve) / (BM * BK * 2 + (bn / 2) * BK * 2));
+}
+
+template <typename T, int BN, bool B_KMAJOR, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                    const EpiParams ep, const int M, const int N, const int K, const int STAGES,
+                    unsigned int* err) {
+  constexpr int BH = BN / 2;                     // B rows (K-major) / columns (MN-major) per CTA
+  constexpr uint32_t A_BYTES = BM * BK * 2;
+  constexpr uint32_t B_BYTES = BH * BK * 2;
+  constexpr uint32_t TMEM_COLS = tmem_cols_for(BN);
+  constexpr uint32_t ACC_STRIDE = TMEM_COLS / 2;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t IDESC = idesc_f16(2 * BM, BN, kBF16, false, !B_KMAJOR);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_bias = reinterpret_cast<float*>(drain_bar + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster_id = static_cast<int>(blockIdx.x >> 1);
+  const int num_clusters = static_cast<int>(gridDim.x >> 1);
+  const int m_tiles = (M + 2 * BM - 1) / (2 * BM);
+  const int n_tiles = (N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int kblocks = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 2 * kEpiWarps);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();   // barriers of both CTAs initialised before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------ TMA producer --
+      tma_prefetch_desc(&tma_a);
+      tma_prefetch_desc(&tma_b);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
+        const int m0 = (tile % m_tiles) * 2 * BM + static_cast<int>(rank) * BM;
+        const int nb0 = (tile / m_tiles) * BN + static_cast<int>(rank) * BH;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, err, kErrGemmProducer)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * (A_BYTES + B_BYTES));
+          const uint32_t leader_full = smem_u32(&full_bar[stage]) & kPeerBitMask;
+          tma_load_2d_pair(sA + stage * A_BYTES, &tma_a, leader_full, kb * BK, m0);
+          if constexpr (B_KMAJOR) {
+            tma_load_2d_pair(sB + stage * B_BYTES, &tma_b, leader_full, kb * BK, nb0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BH / 64; ++j)
+              tma_load_2d_pair(sB + stage * B_BYTES + j * (BK * 128), &tma_b, leader_full, nb0 + j * 64, kb * BK);
+          }
+          if (++stage == static_cast<uint32_t>(STAGES)) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (ok) {
+        // Producer tail: wait until the even CTA's MMA has released every stage
+        // of this CTA once more, so no multicast commit can still be headed
+        // for this CTA's barriers when it exits.
+        for (int i = 0; ok && i < STAGES; ++i) {
+          ok = mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, err, kErrGemmProducer);
+          if (++stage == static_cast<uint32_t>(STAGES)) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      } else {
+        // The loads complete on the even CTA's barrier; give those in flight time to land.
+        const unsigned long long t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 200000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------ MMA issuer (pair) --
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, err, kErrGemmMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * ACC_STRIDE;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, err, kErrGemmMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = sw128_desc(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = B_KMAJOR ? sw128_desc(b_addr + k * 32, 16, 1024)
+                                         : sw128_desc(b_addr + k * 2048, BK * 128, 1024);
+            umma_f16_ss_pair(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(&empty_bar[stage], 0x3);
+          if (++stage == static_cast<uint32_t>(STAGES)) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull_bar[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        umma_commit_pair(drain_bar, 0x1);
+        mbar_drain_wait(drain_bar, 0, 1000000000ull);
+      }
+    }
+  } else {
+    // ----------------------------------------------------------- epilogue --
+    constexpr int kHalf = BN / 2;
+    constexpr int kChunks = kHalf / 32;
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int r = quarter * 32 + lane;
+    const uint32_t leader_tempty = smem_u32(tempty_bar) & kPeerBitMask;
+    uint32_t acc = 0, acc_phase = 0;
+    for (int tile = cluster_id; tile < num_tiles; tile += num_clusters) {
+      const int m0 = (tile % m_tiles) * 2 * BM + static_cast<int>(rank) * BM;
+      const int n0 = (tile / m_tiles) * BN;
+      const int row = m0 + r;
+      const int c0 = n0 + half * kHalf;
+      float* sb = s_bias + (warp - 2) * 128;
+      if (ep.bias != nullptr) {
+        for (int i = lane; i < kHalf; i += 32) {
+          const int col = c0 + i;
+          sb[i] = col < N ? Io<T>::to_f(static_cast<const T*>(ep.bias)[col]) : 0.f;
+        }
+      }
+      ResChunk res[2];
+      load_residual<T>(res[0], row, c0, ep);
+      __syncwarp();
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, err, kErrGemmEpilogue)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * ACC_STRIDE +
+                             half * kHalf;
+      uint32_t v[2][32];
+      tmem_ld_32x32b_x32(t_row, v[0]);
+#pragma unroll 1
+      for (int c = 0; c < kChunks; c += 2) {
+        tmem_ld_wait_regs(v[0]);
+        if (c + 1 < kChunks) {
+          tmem_ld_32x32b_x32(t_row + (c + 1) * 32, v[1]);
+          load_residual<T>(res[1], row, c0 + (c + 1) * 32, ep);
+        }
+        epilogue_chunk<T, EPI>(v[0], row, c0 + c * 32, sb + c * 32, res[0], ep);
+        if (c + 1 < kChunks) {
+          tmem_ld_wait_regs(v[1]);
+          if (c + 2 < kChunks) {
+            tmem_ld_32x32b_x32(t_row + (c + 2) * 32, v[0]);
+            load_residual<T>(res[0], row, c0 + (c + 2) * 32, ep);
+          }
+          epilogue_chunk<T, EPI>(v[1], row, c0 + (c + 1) * 32, sb + (c + 1) * 32, res[1], ep);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(leader_tempty + acc * 8);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();   // neither CTA leaves while the pair's MMAs, TMA bytes or arrivals may target it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------ SIMT path ----
 constexpr int ST = 64;   // output tile
 constexpr int SK = 16;   // K step
@@ -471,25 +707,41 @@ bool encode_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, ui
   return r == CUDA_SUCCESS;
 }
 
-// Estimated cost of one GEMM for a tile width: rounds of persistent tiles
-// times per-tile main-loop cycles (tensor-pipe bound 2*BN per 64-deep K block,
-// shared-memory-read bound 128+BN) plus a fixed per-tile overhead.
-double gemm_cost(int64_t M, int64_t N, int64_t K, int bn, int sms) {
-  const int64_t tiles = ceil_div64(M, BM) * ceil_div64(N, bn);
-  const int64_t rounds = ceil_div64(tiles, sms);
-  const double per_kb = std::max(2.0 * bn, 128.0 + bn);
-  return static_cast<double>(rounds) * (static_cast<double>(ceil_div64(K, BK)) * per_kb + 600.0);
+// Cost model used to pick the kernel when the caller does not: per-CTA
+// cycles of one 64-deep K block are bounded by the tensor pipe (2*BN for both
+// the 128-row and the 256-row pair MMA) and by the operand bytes each CTA must
+// pull from L2 (about 60 B/cycle/SM sustained when every SM streams); tiles
+// are handed out in rounds over the persistent CTAs (pairs), plus a fixed
+// per-tile overhead for fill, drain and the epilogue hand-off.
+struct GemmPlan {
+  int block_n;
+  bool pair;
+};
+
+double gemm_cost(int64_t M, int64_t N, int64_t K, GemmPlan p, int sms) {
+  constexpr double kL2BytesPerCycle = 60.0;
+  const int tile_m = p.pair ? 2 * BM : BM;
+  const int64_t tiles = ceil_div64(M, tile_m) * ceil_div64(N, p.block_n);
+  const int64_t units = p.pair ? sms / 2 : sms;
+  const int64_t rounds = ceil_div64(tiles, units);
+  const double bytes = BM * BK * 2.0 + (p.pair ? p.block_n / 2 : p.block_n) * BK * 2.0;
+  const double per_kb = std::max(2.0 * p.block_n, bytes / kL2BytesPerCycle);
+  return static_cast<double>(rounds) * (static_cast<double>(ceil_div64(K, BK)) * per_kb + 800.0);
 }
 
-int choose_block_n(int64_t M, int64_t N, int64_t K, int sms) {
-  static const int kChoices[] = {256, 192, 128, 64};
-  int best = 256;
+GemmPlan choose_plan(int64_t M, int64_t N, int64_t K, int sms, int block_n, int cta_pair) {
+  static const GemmPlan kChoices[] = {{256, true}, {128, true}, {256, false}, {192, false}, {128, false},
+                                      {64, false}};
+  GemmPlan best{256, true};
   double best_cost = 1e300;
-  for (int bn : kChoices) {
-    const double c = gemm_cost(M, N, K, bn, sms);
-    if (c < best_cost * 0.999) {
-      best_cost = c;
-      best = bn;
+  for (const GemmPlan& c : kChoices) {
+    if (block_n != 0 && c.block_n != block_n) continue;
+    if (cta_pair == 1 && c.pair) continue;
+    if (cta_pair == 2 && !c.pair) continue;
+    const double cost = gemm_cost(M, N, K, c, sms);
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = c;
     }
   }
   return best;
@@ -517,9 +769,56 @@ cudaError_t run_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& 
   return cudaGetLastError();
 }
 
+template <typename T, int BN, bool B_KMAJOR, int EPI>
+cudaError_t run_tc2(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, cudaStream_t s) {
+  auto kern = gemm_tc2_kernel<T, BN, B_KMAJOR, EPI>;
+  constexpr int kMaxStages = pair_stages(BN);
+  constexpr int kStageBytes = BM * BK * 2 + (BN / 2) * BK * 2;
+  static_assert(kMaxStages * kStageBytes + kSmemReserve <= kMaxDynSmem, "shared memory budget");
+  const int stages = (g.stages >= 2 && g.stages <= kMaxStages) ? g.stages : kMaxStages;
+  const int smem = stages * kStageBytes + kSmemReserve;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kMaxStages * kStageBytes + kSmemReserve);
+  if (e != cudaSuccess) return e;
+  // Persistent grid: as many CTA pairs as can be resident (clusters of two
+  // need both SMs of a pair free), capped by the number of 256-row tiles.
+  static int cached_clusters[64] = {};   // per device, for this kernel instantiation
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int max_clusters = device_num_sms() / 2;
+  if (dev >= 0 && dev < 64 && cached_clusters[dev] > 0) {
+    max_clusters = cached_clusters[dev];
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * max_clusters));
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cfg.stream = s;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0 && n < max_clusters)
+      max_clusters = n;
+    cudaGetLastError();
+    if (dev >= 0 && dev < 64) cached_clusters[dev] = max_clusters;
+  }
+  const int64_t tiles = ceil_div64(g.M, 2 * BM) * ceil_div64(g.N, BN);
+  int64_t clusters = g.num_ctas > 1 ? g.num_ctas / 2 : max_clusters;
+  if (clusters > tiles) clusters = tiles;
+  if (clusters < 1) clusters = 1;
+  unsigned int* err = device_error_word();
+  if (err == nullptr) return cudaErrorInvalidDevice;
+  kern<<<static_cast<unsigned>(2 * clusters), kGemmThreads, smem, s>>>(
+      ma, mb, make_epi(g), static_cast<int>(g.M), static_cast<int>(g.N), static_cast<int>(g.K), stages, err);
+  return cudaGetLastError();
+}
+
 template <typename T, bool B_KMAJOR, int EPI>
-cudaError_t dispatch_epi(const GemmArgs& g, int bn, const CUtensorMap& ma, const CUtensorMap& mb, cudaStream_t s) {
-  switch (bn) {
+cudaError_t dispatch_epi(const GemmArgs& g, GemmPlan plan, const CUtensorMap& ma, const CUtensorMap& mb,
+                         cudaStream_t s) {
+  if (plan.pair) {
+    return plan.block_n == 128 ? run_tc2<T, 128, B_KMAJOR, EPI>(g, ma, mb, s)
+                               : run_tc2<T, 256, B_KMAJOR, EPI>(g, ma, mb, s);
+  }
+  switch (plan.block_n) {
     case 64: return run_tc<T, 64, B_KMAJOR, EPI>(g, ma, mb, s);
     case 128: return run_tc<T, 128, B_KMAJOR, EPI>(g, ma, mb, s);
     case 192: return run_tc<T, 192, B_KMAJOR, EPI>(g, ma, mb, s);
@@ -528,16 +827,18 @@ cudaError_t dispatch_epi(const GemmArgs& g, int bn, const CUtensorMap& ma, const
 }
 
 template <typename T, bool B_KMAJOR>
-cudaError_t dispatch_bn(const GemmArgs& g, int bn, cudaStream_t s) {
+cudaError_t dispatch_plan(const GemmArgs& g, GemmPlan plan, cudaStream_t s) {
   CUtensorMap ma, mb;
+  // B rows (K-major) or columns (MN-major) loaded by one CTA per K block.
+  const int b_box = plan.pair ? plan.block_n / 2 : plan.block_n;
   if (!encode_2d(&ma, g.A, g.dtype, g.K, g.M, g.lda * 2, BK, BM)) return cudaErrorInvalidValue;
-  const bool ok_b = B_KMAJOR ? encode_2d(&mb, g.B, g.dtype, g.K, g.N, g.ldb * 2, BK, bn)
+  const bool ok_b = B_KMAJOR ? encode_2d(&mb, g.B, g.dtype, g.K, g.N, g.ldb * 2, BK, b_box)
                              : encode_2d(&mb, g.B, g.dtype, g.N, g.K, g.ldb * 2, 64, BK);
   if (!ok_b) return cudaErrorInvalidValue;
   switch (epi_mode_for(g.act)) {
-    case kEpiPlain: return dispatch_epi<T, B_KMAJOR, kEpiPlain>(g, bn, ma, mb, s);
-    case kEpiGeluTanh: return dispatch_epi<T, B_KMAJOR, kEpiGeluTanh>(g, bn, ma, mb, s);
-    default: return dispatch_epi<T, B_KMAJOR, kEpiAnyAct>(g, bn, ma, mb, s);
+    case kEpiPlain: return dispatch_epi<T, B_KMAJOR, kEpiPlain>(g, plan, ma, mb, s);
+    case kEpiGeluTanh: return dispatch_epi<T, B_KMAJOR, kEpiGeluTanh>(g, plan, ma, mb, s);
+    default: return dispatch_epi<T, B_KMAJOR, kEpiAnyAct>(g, plan, ma, mb, s);
   }
 }
 
@@ -553,12 +854,17 @@ bool gemm_tc_supported(const GemmArgs& g) {
 }
 
 cudaError_t launch_gemm_tcgen05(const GemmArgs& g, cudaStream_t stream) {
+  // Requested tile: block_n in {64,128,192,256} (pairs take 128 or 256), cta_pair 1 = single CTA, 2 = pair.
   int bn = g.block_n;
-  if (bn != 64 && bn != 128 && bn != 192 && bn != 256) bn = choose_block_n(g.M, g.N, g.K, device_num_sms());
+  if (bn != 64 && bn != 128 && bn != 192 && bn != 256) bn = 0;
+  int pair = g.cta_pair;
+  if (bn == 64 || bn == 192) pair = 1;
+  const GemmPlan plan = choose_plan(g.M, g.N, g.K, device_num_sms(), bn, pair);
   const bool kmajor = g.b_layout == LUNARA_B_NK;
   if (g.dtype == LUNARA_BF16)
-    return kmajor ? dispatch_bn<__nv_bfloat16, true>(g, bn, stream) : dispatch_bn<__nv_bfloat16, false>(g, bn, stream);
-  return kmajor ? dispatch_bn<__half, true>(g, bn, stream) : dispatch_bn<__half, false>(g, bn, stream);
+    return kmajor ? dispatch_plan<__nv_bfloat16, true>(g, plan, stream)
+                  : dispatch_plan<__nv_bfloat16, false>(g, plan, stream);
+  return kmajor ? dispatch_plan<__half, true>(g, plan, stream) : dispatch_plan<__half, false>(g, plan, stream);
 }
 
 cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t stream) {

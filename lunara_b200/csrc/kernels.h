@@ -44,6 +44,7 @@ struct GemmArgs {
   int block_n;   // 0 = auto
   int stages;    // 0 = auto
   int num_ctas;  // 0 = auto
+  int cta_pair;  // 0 = auto, 1 = single-CTA tiles, 2 = CTA-pair (cta_group::2) tiles
 };
 
 // True when the tcgen05/TMA path accepts the shapes, strides and pointers.

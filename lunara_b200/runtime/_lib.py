@@ -30,10 +30,10 @@ _pi64 = ctypes.POINTER(ctypes.c_int64)
 
 
 class GemmConfig(ctypes.Structure):
-    """``lunara_gemm_config``: block_n, stages, num_ctas (0 = automatic)."""
+    """``lunara_gemm_config``: block_n, stages, num_ctas, cta_pair (0 = automatic)."""
 
     _fields_ = [("block_n", ctypes.c_int32), ("stages", ctypes.c_int32),
-                ("num_ctas", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+                ("num_ctas", ctypes.c_int32), ("cta_pair", ctypes.c_int32)]
 
 
 SIGNATURES = {

@@ -62,12 +62,14 @@ def _require_cuda(*ts: Optional[torch.Tensor]) -> None:
 def gemm(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor] = None,
          bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
          activation=None, b_layout: str = "kn", block_n: int = 0, stages: int = 0,
-         num_ctas: int = 0) -> torch.Tensor:
+         num_ctas: int = 0, cta_pair: int = 0) -> torch.Tensor:
     """C = act(A @ B + bias) + residual.
 
     ``b_layout="kn"``: B is [K, N] (the reference launcher's B);
     ``b_layout="nk"``: B is [N, K] (a Linear weight, C = A @ B^T).
     A, B, C and residual need a unit inner stride; leading dimensions are free.
+    ``block_n`` / ``stages`` / ``num_ctas`` / ``cta_pair`` (1 single-CTA tiles,
+    2 CTA-pair tiles) override the automatic tile choice; 0 means automatic.
     """
     _require_cuda(A, B, C, bias, residual)
     assert A.dim() == 2 and B.dim() == 2, "GEMM operands must be 2-D"
@@ -94,7 +96,7 @@ def gemm(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor] = None,
         assert residual.shape == (M, N) and residual.dtype == A.dtype, "residual must be [M, N]"
         assert residual.stride(1) == 1 or N == 1, "residual needs a unit inner stride"
         ldr = residual.stride(0)
-    cfg = _lib.GemmConfig(block_n, stages, num_ctas, 0)
+    cfg = _lib.GemmConfig(block_n, stages, num_ctas, cta_pair)
     lib = _lib.load()
     _lib.check(lib.lunara_gemm(A.data_ptr(), B.data_ptr(), C.data_ptr(), _ptr(bias), _ptr(residual),
                                M, N, K, max(A.stride(0), K), max(B.stride(0), 1), max(C.stride(0), N), ldr,

@@ -36,8 +36,31 @@ def _mk(M, N, K, dtype, seed, layout="kn", scale=1.0):
 def test_gemm_tile_widths(dtype, layout, bn):
     M, N, K = 256, 512, 192
     a, b, _, _ = _mk(M, N, K, dtype, bn, layout, scale=0.5)
-    c = _ops().gemm(a.cuda(), b.cuda(), b_layout=layout, block_n=bn)
+    c = _ops().gemm(a.cuda(), b.cuda(), b_layout=layout, block_n=bn, cta_pair=1)
     check_close(c, oracle.gemm(a, b, b_layout=layout), dtype, f"gemm bn={bn} {layout}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("layout", ["kn", "nk"])
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm_cta_pair_tiles(dtype, layout, bn):
+    """256-row tiles computed by a CTA pair (cta_group::2 MMA), several tiles per pair."""
+    M, N, K = 1024, 768, 320
+    a, b, bias, res = _mk(M, N, K, dtype, bn + 1, layout, scale=0.5)
+    ops = _ops()
+    c = ops.gemm(a.cuda(), b.cuda(), bias=bias.cuda(), residual=res.cuda(), b_layout=layout, block_n=bn,
+                 cta_pair=2, num_ctas=4)
+    check_close(c, oracle.gemm(a, b, bias, residual=res, b_layout=layout), dtype, f"pair gemm bn={bn} {layout}")
+
+
+@pytest.mark.parametrize("layout", ["kn", "nk"])
+@pytest.mark.parametrize("M,N,K", [(300, 136, 72), (129, 512, 1000), (600, 264, 64)])
+def test_gemm_cta_pair_ragged(layout, M, N, K):
+    a, b, bias, _ = _mk(M, N, K, torch.float16, M + N, layout, scale=0.5)
+    for act in (None, "gelu_tanh", "relu"):
+        c = _ops().gemm(a.cuda(), b.cuda(), bias=bias.cuda(), activation=act, b_layout=layout, cta_pair=2)
+        check_close(c, oracle.gemm(a, b, bias, activation=act, b_layout=layout), torch.float16,
+                    f"pair gemm {M}x{N}x{K} {act}")
 
 
 @pytest.mark.parametrize("layout", ["kn", "nk"])
@@ -65,7 +88,7 @@ def test_gemm_many_tiles_per_cta_and_stages():
     a, b, bias, _ = _mk(M, N, K, torch.float16, 12, "kn", scale=0.5)
     ref = oracle.gemm(a, b, bias)
     for bn, stages, ctas in [(128, 2, 3), (256, 3, 5), (64, 8, 1), (192, 5, 7)]:
-        c = ops.gemm(a.cuda(), b.cuda(), bias=bias.cuda(), block_n=bn, stages=stages, num_ctas=ctas)
+        c = ops.gemm(a.cuda(), b.cuda(), bias=bias.cuda(), block_n=bn, stages=stages, num_ctas=ctas, cta_pair=1)
         check_close(c, ref, torch.float16, f"gemm bn={bn} stages={stages} ctas={ctas}")
 
 
