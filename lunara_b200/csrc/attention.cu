@@ -282,11 +282,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int i = 0; i < 32; ++i)
             if (c * 32 + i >= lim) sc[c][i] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;
+      // Row maximum with eight independent partial maxima (short dependency chains).
+      float mxp[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) mxp[t] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sc[c][i]));
+        for (int i = 0; i < 32; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sc[c][i]));
+      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
       const float m_cand = mx * sl2;
       // P of the previous block must have been consumed (and O updated) before
       // P is overwritten and O is touched.
@@ -317,7 +322,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       const float m_off = (m_used == -INFINITY) ? 0.f : m_used;
       // P = exp2(S * scale * log2e - m), row sum, P -> swizzled K-major smem tile.
-      float sum = 0.f;
+      float sump[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
@@ -325,7 +330,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int i = 0; i < 32; i += 2) {
           const float e0 = ex2_approx(fmaf(__uint_as_float(sc[c][i]), sl2, -m_off));
           const float e1 = ex2_approx(fmaf(__uint_as_float(sc[c][i + 1]), sl2, -m_off));
-          sum += e0 + e1;
+          sump[(i >> 1) & 7] += e0 + e1;
           pk[i / 2] = Io<T>::pack2(e0, e1);
         }
         uint8_t* chunk = myP + (c / 2) * kTileBytes + r * 128;
@@ -336,7 +341,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
       }
-      l += sum;
+      l += ((sump[0] + sump[1]) + (sump[2] + sump[3])) + ((sump[4] + sump[5]) + (sump[6] + sump[7]));
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_ready[w]);
