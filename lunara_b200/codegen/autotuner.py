@@ -39,7 +39,7 @@ BLOCK_M = 128
 BLOCK_K = 64
 _BLOCK_N_CHOICES = [64, 128, 192, 256]
 _SMEM_LIMIT = 232448          # 227 KB opt-in dynamic shared memory per CTA
-_SMEM_RESERVED = 6144         # barriers, bias staging, 1 KB alignment slack
+_SMEM_RESERVED = 22528        # barriers, bias and output staging, 1 KB alignment slack
 
 
 def max_stages(block_n: int, elem_bytes: int = 2) -> int:

@@ -47,6 +47,7 @@ constexpr int kProducerRegs = 56;
 constexpr int kSoftmaxRegs = 224;
 static_assert(128 * kProducerRegs + 256 * kSoftmaxRegs <= kAttnThreads * kLaunchRegs, "register split");
 constexpr float kRescaleLog2 = 8.0f;
+constexpr int kPolyEvery = 4;   // exponentials evaluated by polynomial: one pair in four
 constexpr uint32_t kTileBytes = 128 * 128;  // one [128 x 64] 16-bit tile
 constexpr int kAttnSmem = 2 * kTileBytes + 2 * kKvStages * kTileBytes + 2 * 2 * kTileBytes + 256 + 1024;
 constexpr uint32_t kAttnTmemCols = 512;
@@ -328,8 +329,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float e0 = ex2_approx(fmaf(__uint_as_float(sc[c][i]), sl2, -m_off));
-          const float e1 = ex2_approx(fmaf(__uint_as_float(sc[c][i + 1]), sl2, -m_off));
+          // One pair in kPolyEvery is computed on the FMA pipe, the rest on MUFU,
+          // so that both pipes share the exponentials.
+          const bool poly = ((c * 16 + i / 2) % kPolyEvery) == kPolyEvery - 1;
+          const float x0 = fmaf(__uint_as_float(sc[c][i]), sl2, -m_off);
+          const float x1 = fmaf(__uint_as_float(sc[c][i + 1]), sl2, -m_off);
+          const float e0 = poly ? ex2_poly(x0) : ex2_approx(x0);
+          const float e1 = poly ? ex2_poly(x1) : ex2_approx(x1);
           sump[(i >> 1) & 7] += e0 + e1;
           pk[i / 2] = Io<T>::pack2(e0, e1);
         }

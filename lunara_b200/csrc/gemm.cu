@@ -10,7 +10,9 @@
 //                 each): tcgen05.ld of the accumulator one 32-column chunk
 //                 ahead (thread = row), bias (staged per warp in shared
 //                 memory) + activation + residual (loaded one chunk ahead) in
-//                 fp32, one rounding, 16-byte global stores
+//                 fp32, one rounding; each warp stages its 32 x 32 output
+//                 chunk in shared memory (64-byte swizzle) and writes it with
+//                 one TMA store (direct 16-byte stores when C is unaligned)
 //   Two TMEM accumulators (2 x BN fp32 columns) let the epilogue of tile i
 //   overlap the main loop of tile i+1. No TMA multicast is used anywhere (the
 //   same kernel runs in multi-GPU jobs).
@@ -23,6 +25,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstring>
 #include <type_traits>
 
 #include "common.cuh"
@@ -37,7 +40,8 @@ constexpr int kEpiWarps = 8;        // two warps per TMEM lane quarter, each own
 constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kGemmThreads = 64 + kEpiThreads;
 constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in limit per block on sm_100
-constexpr int kSmemReserve = 6144;   // barriers, bias staging (8 warps x 128 fp32), 1 KB alignment slack
+constexpr int kStageC = 2048;       // per epilogue warp: one 32 x 32 16-bit output chunk
+constexpr int kSmemReserve = 6144 + kEpiWarps * kStageC;  // barriers, bias staging, output staging, alignment
 
 struct EpiParams {
   void* C;
@@ -46,7 +50,8 @@ struct EpiParams {
   int64_t ldc, ldr;
   int M, N;
   int act;
-  int vec_ok;  // C / residual / bias allow 16-byte accesses
+  int vec_ok;     // C / residual / bias allow 16-byte accesses
+  int tma_store;  // C written through the tensor map (tiles staged in shared memory)
 };
 
 __host__ __device__ constexpr int gemm_stages(int bn) {
@@ -163,10 +168,127 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&acc)[32], int ro
   }
 }
 
+// Bias + activation + residual of one 32-column chunk of one row, rounded and
+// packed as 16 pairs of 16-bit values.
+template <typename T, int EPI>
+__device__ __forceinline__ void epilogue_pack(const uint32_t (&acc)[32], int row, int col0, const float* s_bias,
+                                              const ResChunk& rc, const EpiParams& ep, uint32_t (&pk)[16]) {
+  float f[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(acc[i]);
+  if (ep.bias != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) f[i] += s_bias[i];
+  }
+  if constexpr (EPI == kEpiGeluTanh) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) f[i] = apply_act(f[i], LUNARA_ACT_GELU_TANH);
+  } else if constexpr (EPI == kEpiAnyAct) {
+    act_chunk_any(f, ep.act);
+  }
+  if (ep.residual != nullptr && row < ep.M) {
+    if (col0 + 32 <= ep.N) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t w[4] = {rc.q[q].x, rc.q[q].y, rc.q[q].z, rc.q[q].w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float2 p = Io<T>::unpack2(w[h]);
+          f[q * 8 + 2 * h] += p.x;
+          f[q * 8 + 2 * h + 1] += p.y;
+        }
+      }
+    } else {
+      const T* r = static_cast<const T*>(ep.residual) + static_cast<int64_t>(row) * ep.ldr + col0;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < ep.N) f[i] += Io<T>::to_f(r[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) pk[i] = Io<T>::pack2(f[2 * i], f[2 * i + 1]);
+}
+
+// One 32-row x 32-column output chunk of a warp: either staged in the warp's
+// shared buffer with the 64-byte swizzle (16-byte chunk q of row r at slot
+// q ^ ((r >> 1) & 3), conflict-free) and written by one TMA store that clips
+// rows >= M and columns >= N, or stored directly by each thread.
+template <typename T, int EPI>
+__device__ __forceinline__ void epilogue_out(const uint32_t (&acc)[32], int row, int col0, int row0_warp,
+                                             const float* s_bias, const ResChunk& rc, const EpiParams& ep,
+                                             const CUtensorMap* tma_c, uint8_t* s_stage, int lane) {
+  if (ep.tma_store) {
+    uint32_t pk[16];
+    epilogue_pack<T, EPI>(acc, row, col0, s_bias, rc, ep, pk);
+    if (lane == 0) bulk_wait_group_read<0>();   // the previous chunk's store has read the buffer
+    __syncwarp();
+    uint8_t* dst = s_stage + lane * 64;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4*>(dst + ((q ^ ((lane >> 1) & 3)) << 4)) =
+          make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tma_c, s_stage, col0, row0_warp);
+      bulk_commit_group();
+    }
+  } else {
+    epilogue_chunk<T, EPI>(acc, row, col0, s_bias, rc, ep);
+  }
+}
+
+// The epilogue of one accumulator tile for one warp: `kHalf` columns starting at
+// c0 for the 32 rows starting at row0_warp (this lane's row = row0_warp + lane),
+// read from TMEM at t_row one 32-column chunk ahead of their use.
+template <typename T, int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row0_warp, int c0, const float* sb,
+                                              const EpiParams& ep, const CUtensorMap* tma_c, uint8_t* s_stage,
+                                              int lane) {
+  constexpr int kHalf = BN / 2;
+  constexpr int kChunks = kHalf / 32;
+  const int row = row0_warp + lane;
+  ResChunk res[2];
+  load_residual<T>(res[0], row, c0, ep);
+  // Chunks are processed in pairs (two register buffers, compile-time
+  // indices); the loop itself is not unrolled to keep the code small.
+  uint32_t v[2][32];
+  tmem_ld_32x32b_x32(t_row, v[0]);
+#pragma unroll 1
+  for (int c = 0; c < kChunks; c += 2) {
+    tmem_ld_wait_regs(v[0]);
+    if (c + 1 < kChunks) {
+      tmem_ld_32x32b_x32(t_row + (c + 1) * 32, v[1]);
+      load_residual<T>(res[1], row, c0 + (c + 1) * 32, ep);
+    }
+    epilogue_out<T, EPI>(v[0], row, c0 + c * 32, row0_warp, sb + c * 32, res[0], ep, tma_c, s_stage, lane);
+    if (c + 1 < kChunks) {
+      tmem_ld_wait_regs(v[1]);
+      if (c + 2 < kChunks) {
+        tmem_ld_32x32b_x32(t_row + (c + 2) * 32, v[0]);
+        load_residual<T>(res[0], row, c0 + (c + 2) * 32, ep);
+      }
+      epilogue_out<T, EPI>(v[1], row, c0 + (c + 1) * 32, row0_warp, sb + (c + 1) * 32, res[1], ep, tma_c,
+                           s_stage, lane);
+    }
+  }
+}
+
+// Stage this warp's slice of the bias (fp32) in its own shared-memory region;
+// only this warp reads it, so __syncwarp orders writes and reads.
+template <typename T>
+__device__ __forceinline__ void stage_bias(float* sb, int c0, int count, const EpiParams& ep, int lane) {
+  if (ep.bias == nullptr) return;
+  for (int i = lane; i < count; i += 32) {
+    const int col = c0 + i;
+    sb[i] = col < ep.N ? Io<T>::to_f(static_cast<const T*>(ep.bias)[col]) : 0.f;
+  }
+}
+
 template <typename T, int BN, bool B_KMAJOR, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                   const EpiParams ep, const int M, const int N, const int K, const int STAGES,
+                   const __grid_constant__ CUtensorMap tma_c, const EpiParams ep, const int M, const int N, const int K, const int STAGES,
                    unsigned int* err) {
   // STAGES (ring depth) is chosen on the host, 2 <= STAGES <= gemm_stages(BN);
   // the dynamic shared-memory size is sized for it.
@@ -181,7 +303,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* sC = sB + STAGES * B_BYTES;   // kEpiWarps x kStageC output staging (1024-aligned)
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sC + kEpiWarps * kStageC);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -309,55 +432,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // 32*q .. 32*q+31 of the tile); warps 2-5 take the first half of the
     // tile's columns, warps 6-9 the second half.
     constexpr int kHalf = BN / 2;
-    constexpr int kChunks = kHalf / 32;
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
-    const int r = quarter * 32 + lane;
+    float* sb = s_bias + (warp - 2) * 128;
+    uint8_t* s_stage = sC + (warp - 2) * kStageC;
     uint32_t acc = 0, acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int m0 = (tile % m_tiles) * BM;
       const int n0 = (tile / m_tiles) * BN;
-      const int row = m0 + r;
       const int c0 = n0 + half * kHalf;
-      // Stage this warp's slice of the bias in its own shared-memory region
-      // (fp32) while the MMAs run; only this warp reads it, so __syncwarp
-      // orders the writes before the reads and the previous tile's reads
-      // before these writes.
-      float* sb = s_bias + (warp - 2) * 128;
-      if (ep.bias != nullptr) {
-        for (int i = lane; i < kHalf; i += 32) {
-          const int col = c0 + i;
-          sb[i] = col < N ? Io<T>::to_f(static_cast<const T*>(ep.bias)[col]) : 0.f;
-        }
-      }
-      ResChunk res[2];
-      load_residual<T>(res[0], row, c0, ep);
+      stage_bias<T>(sb, c0, kHalf, ep, lane);
       __syncwarp();
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, err, kErrGemmEpilogue)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * ACC_STRIDE +
                              half * kHalf;
-      // Chunks are processed in pairs (two register buffers, compile-time
-      // indices); the loop itself is not unrolled to keep the code small.
-      uint32_t v[2][32];
-      tmem_ld_32x32b_x32(t_row, v[0]);
-#pragma unroll 1
-      for (int c = 0; c < kChunks; c += 2) {
-        tmem_ld_wait_regs(v[0]);
-        if (c + 1 < kChunks) {
-          tmem_ld_32x32b_x32(t_row + (c + 1) * 32, v[1]);
-          load_residual<T>(res[1], row, c0 + (c + 1) * 32, ep);
-        }
-        epilogue_chunk<T, EPI>(v[0], row, c0 + c * 32, sb + c * 32, res[0], ep);
-        if (c + 1 < kChunks) {
-          tmem_ld_wait_regs(v[1]);
-          if (c + 2 < kChunks) {
-            tmem_ld_32x32b_x32(t_row + (c + 2) * 32, v[0]);
-            load_residual<T>(res[0], row, c0 + (c + 2) * 32, ep);
-          }
-          epilogue_chunk<T, EPI>(v[1], row, c0 + (c + 1) * 32, sb + (c + 1) * 32, res[1], ep);
-        }
-      }
+      epilogue_tile<T, BN, EPI>(t_row, m0 + quarter * 32, c0, sb, ep, &tma_c, s_stage, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
@@ -366,6 +456,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         acc_phase ^= 1u;
       }
     }
+    if (lane == 0) bulk_wait_group_all();   // output stores done before the CTA exits
   }
 
   tc_fence_before();
@@ -397,7 +488,7 @@ __host__ __device__ constexpr int pair_stages(int bn) {
 template <typename T, int BN, bool B_KMAJOR, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                    const EpiParams ep, const int M, const int N, const int K, const int STAGES,
+                    const __grid_constant__ CUtensorMap tma_c, const EpiParams ep, const int M, const int N, const int K, const int STAGES,
                     unsigned int* err) {
   constexpr int BH = BN / 2;                     // B rows (K-major) / columns (MN-major) per CTA
   constexpr uint32_t A_BYTES = BM * BK * 2;
@@ -411,7 +502,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* sC = sB + STAGES * B_BYTES;   // kEpiWarps x kStageC output staging (1024-aligned)
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sC + kEpiWarps * kStageC);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -550,50 +642,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   } else {
     // ----------------------------------------------------------- epilogue --
     constexpr int kHalf = BN / 2;
-    constexpr int kChunks = kHalf / 32;
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
-    const int r = quarter * 32 + lane;
     const uint32_t leader_tempty = smem_u32(tempty_bar) & kPeerBitMask;
+    float* sb = s_bias + (warp - 2) * 128;
+    uint8_t* s_stage = sC + (warp - 2) * kStageC;
     uint32_t acc = 0, acc_phase = 0;
     for (int tile = cluster_id; tile < num_tiles; tile += num_clusters) {
       const int m0 = (tile % m_tiles) * 2 * BM + static_cast<int>(rank) * BM;
       const int n0 = (tile / m_tiles) * BN;
-      const int row = m0 + r;
       const int c0 = n0 + half * kHalf;
-      float* sb = s_bias + (warp - 2) * 128;
-      if (ep.bias != nullptr) {
-        for (int i = lane; i < kHalf; i += 32) {
-          const int col = c0 + i;
-          sb[i] = col < N ? Io<T>::to_f(static_cast<const T*>(ep.bias)[col]) : 0.f;
-        }
-      }
-      ResChunk res[2];
-      load_residual<T>(res[0], row, c0, ep);
+      stage_bias<T>(sb, c0, kHalf, ep, lane);
       __syncwarp();
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, err, kErrGemmEpilogue)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * ACC_STRIDE +
                              half * kHalf;
-      uint32_t v[2][32];
-      tmem_ld_32x32b_x32(t_row, v[0]);
-#pragma unroll 1
-      for (int c = 0; c < kChunks; c += 2) {
-        tmem_ld_wait_regs(v[0]);
-        if (c + 1 < kChunks) {
-          tmem_ld_32x32b_x32(t_row + (c + 1) * 32, v[1]);
-          load_residual<T>(res[1], row, c0 + (c + 1) * 32, ep);
-        }
-        epilogue_chunk<T, EPI>(v[0], row, c0 + c * 32, sb + c * 32, res[0], ep);
-        if (c + 1 < kChunks) {
-          tmem_ld_wait_regs(v[1]);
-          if (c + 2 < kChunks) {
-            tmem_ld_32x32b_x32(t_row + (c + 2) * 32, v[0]);
-            load_residual<T>(res[0], row, c0 + (c + 2) * 32, ep);
-          }
-          epilogue_chunk<T, EPI>(v[1], row, c0 + (c + 1) * 32, sb + (c + 1) * 32, res[1], ep);
-        }
-      }
+      epilogue_tile<T, BN, EPI>(t_row, m0 + quarter * 32, c0, sb, ep, &tma_c, s_stage, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_tempty + acc * 8);
@@ -602,6 +667,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         acc_phase ^= 1u;
       }
     }
+    if (lane == 0) bulk_wait_group_all();   // output stores done before the CTA exits
   }
 
   __syncwarp();
@@ -688,11 +754,13 @@ EpiParams make_epi(const GemmArgs& g) {
   ep.act = g.act;
   ep.vec_ok = al16(g.C) && (g.ldc % 8 == 0) && (g.bias == nullptr || al16(g.bias)) &&
               (g.residual == nullptr || (al16(g.residual) && g.ldr % 8 == 0));
+  ep.tma_store = 0;
   return ep;
 }
 
 bool encode_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer, uint64_t stride_bytes,
-               uint32_t box_inner, uint32_t box_outer) {
+               uint32_t box_inner, uint32_t box_outer,
+               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(tensor_map_encoder());
   if (encode == nullptr) return false;
   const cuuint64_t dims[2] = {inner, outer};
@@ -702,7 +770,7 @@ bool encode_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, ui
   const CUtensorMapDataType dt =
       dtype == LUNARA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const CUresult r = encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -748,7 +816,8 @@ GemmPlan choose_plan(int64_t M, int64_t N, int64_t K, int sms, int block_n, int 
 }
 
 template <typename T, int BN, bool B_KMAJOR, int EPI>
-cudaError_t run_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, cudaStream_t s) {
+cudaError_t run_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+                   const EpiParams& ep, cudaStream_t s) {
   auto kern = gemm_tc_kernel<T, BN, B_KMAJOR, EPI>;
   constexpr int kMaxStages = gemm_stages(BN);
   static_assert(gemm_smem_bytes(BN, kMaxStages) <= kMaxDynSmem, "shared memory budget");
@@ -763,14 +832,15 @@ cudaError_t run_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& 
   if (grid > tiles) grid = tiles;
   unsigned int* err = device_error_word();
   if (err == nullptr) return cudaErrorInvalidDevice;
-  kern<<<static_cast<unsigned>(grid), kGemmThreads, smem, s>>>(ma, mb, make_epi(g), static_cast<int>(g.M),
+  kern<<<static_cast<unsigned>(grid), kGemmThreads, smem, s>>>(ma, mb, mc, ep, static_cast<int>(g.M),
                                                                static_cast<int>(g.N), static_cast<int>(g.K),
                                                                stages, err);
   return cudaGetLastError();
 }
 
 template <typename T, int BN, bool B_KMAJOR, int EPI>
-cudaError_t run_tc2(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, cudaStream_t s) {
+cudaError_t run_tc2(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+                    const EpiParams& ep, cudaStream_t s) {
   auto kern = gemm_tc2_kernel<T, BN, B_KMAJOR, EPI>;
   constexpr int kMaxStages = pair_stages(BN);
   constexpr int kStageBytes = BM * BK * 2 + (BN / 2) * BK * 2;
@@ -807,22 +877,22 @@ cudaError_t run_tc2(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap&
   unsigned int* err = device_error_word();
   if (err == nullptr) return cudaErrorInvalidDevice;
   kern<<<static_cast<unsigned>(2 * clusters), kGemmThreads, smem, s>>>(
-      ma, mb, make_epi(g), static_cast<int>(g.M), static_cast<int>(g.N), static_cast<int>(g.K), stages, err);
+      ma, mb, mc, ep, static_cast<int>(g.M), static_cast<int>(g.N), static_cast<int>(g.K), stages, err);
   return cudaGetLastError();
 }
 
 template <typename T, bool B_KMAJOR, int EPI>
 cudaError_t dispatch_epi(const GemmArgs& g, GemmPlan plan, const CUtensorMap& ma, const CUtensorMap& mb,
-                         cudaStream_t s) {
+                         const CUtensorMap& mc, const EpiParams& ep, cudaStream_t s) {
   if (plan.pair) {
-    return plan.block_n == 128 ? run_tc2<T, 128, B_KMAJOR, EPI>(g, ma, mb, s)
-                               : run_tc2<T, 256, B_KMAJOR, EPI>(g, ma, mb, s);
+    return plan.block_n == 128 ? run_tc2<T, 128, B_KMAJOR, EPI>(g, ma, mb, mc, ep, s)
+                               : run_tc2<T, 256, B_KMAJOR, EPI>(g, ma, mb, mc, ep, s);
   }
   switch (plan.block_n) {
-    case 64: return run_tc<T, 64, B_KMAJOR, EPI>(g, ma, mb, s);
-    case 128: return run_tc<T, 128, B_KMAJOR, EPI>(g, ma, mb, s);
-    case 192: return run_tc<T, 192, B_KMAJOR, EPI>(g, ma, mb, s);
-    default: return run_tc<T, 256, B_KMAJOR, EPI>(g, ma, mb, s);
+    case 64: return run_tc<T, 64, B_KMAJOR, EPI>(g, ma, mb, mc, ep, s);
+    case 128: return run_tc<T, 128, B_KMAJOR, EPI>(g, ma, mb, mc, ep, s);
+    case 192: return run_tc<T, 192, B_KMAJOR, EPI>(g, ma, mb, mc, ep, s);
+    default: return run_tc<T, 256, B_KMAJOR, EPI>(g, ma, mb, mc, ep, s);
   }
 }
 
@@ -835,10 +905,17 @@ cudaError_t dispatch_plan(const GemmArgs& g, GemmPlan plan, cudaStream_t s) {
   const bool ok_b = B_KMAJOR ? encode_2d(&mb, g.B, g.dtype, g.K, g.N, g.ldb * 2, BK, b_box)
                              : encode_2d(&mb, g.B, g.dtype, g.N, g.K, g.ldb * 2, 64, BK);
   if (!ok_b) return cudaErrorInvalidValue;
+  // Output through TMA stores of 32 x 32 chunks (64-byte swizzle) when C allows
+  // 16-byte accesses; otherwise each thread stores its row directly.
+  EpiParams ep = make_epi(g);
+  CUtensorMap mc;
+  std::memset(&mc, 0, sizeof(mc));
+  if (ep.vec_ok && encode_2d(&mc, g.C, g.dtype, g.N, g.M, g.ldc * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+    ep.tma_store = 1;
   switch (epi_mode_for(g.act)) {
-    case kEpiPlain: return dispatch_epi<T, B_KMAJOR, kEpiPlain>(g, plan, ma, mb, s);
-    case kEpiGeluTanh: return dispatch_epi<T, B_KMAJOR, kEpiGeluTanh>(g, plan, ma, mb, s);
-    default: return dispatch_epi<T, B_KMAJOR, kEpiAnyAct>(g, plan, ma, mb, s);
+    case kEpiPlain: return dispatch_epi<T, B_KMAJOR, kEpiPlain>(g, plan, ma, mb, mc, ep, s);
+    case kEpiGeluTanh: return dispatch_epi<T, B_KMAJOR, kEpiGeluTanh>(g, plan, ma, mb, mc, ep, s);
+    default: return dispatch_epi<T, B_KMAJOR, kEpiAnyAct>(g, plan, ma, mb, mc, ep, s);
   }
 }
 
