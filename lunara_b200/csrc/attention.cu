@@ -47,7 +47,10 @@ constexpr int kProducerRegs = 56;
 constexpr int kSoftmaxRegs = 224;
 static_assert(128 * kProducerRegs + 256 * kSoftmaxRegs <= kAttnThreads * kLaunchRegs, "register split");
 constexpr float kRescaleLog2 = 8.0f;
-constexpr int kPolyEvery = 4;   // exponentials evaluated by polynomial: one pair in four
+// Exponential pairs evaluated on the FMA pipe instead of MUFU (one pair in
+// kPolyEvery; 0 = none). Measured on B200 at head dim 64: moving a quarter of
+// them lowered throughput (the exp unit is not the limit), so it is off.
+constexpr int kPolyEvery = 0;
 constexpr uint32_t kTileBytes = 128 * 128;  // one [128 x 64] 16-bit tile
 constexpr int kAttnSmem = 2 * kTileBytes + 2 * kKvStages * kTileBytes + 2 * 2 * kTileBytes + 256 + 1024;
 constexpr uint32_t kAttnTmemCols = 512;
@@ -331,7 +334,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int i = 0; i < 32; i += 2) {
           // One pair in kPolyEvery is computed on the FMA pipe, the rest on MUFU,
           // so that both pipes share the exponentials.
-          const bool poly = ((c * 16 + i / 2) % kPolyEvery) == kPolyEvery - 1;
+          const bool poly = kPolyEvery > 0 && ((c * 16 + i / 2) % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1;
           const float x0 = fmaf(__uint_as_float(sc[c][i]), sl2, -m_off);
           const float x1 = fmaf(__uint_as_float(sc[c][i + 1]), sl2, -m_off);
           const float e0 = poly ? ex2_poly(x0) : ex2_approx(x0);
