@@ -185,7 +185,12 @@ def bench_block(args, rank, world, device):
     blk.x.copy_(x.half().view(batch * seq, 768).to(device))
     flops = block_flops(batch * seq, seq)
 
-    # Events around every kernel, captured inside the graph (external events).
+    # Timed graph: the seven kernels alone (adjacent kernel nodes keep their
+    # programmatic-launch overlap). A second copy of the graph with an event
+    # between kernels (external events) gives per-kernel durations; it is
+    # replayed in its own loop after the timed one, since event nodes between
+    # kernels serialise them.
+    runner = GraphRunner(lambda: blk.run_kernels())
     n_ev = len(KERNEL_ORDER) + 1
     evs = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_ev)]
     idx = {name: i for i, name in enumerate(KERNEL_ORDER)}
@@ -197,12 +202,10 @@ def bench_block(args, rank, world, device):
             evs[idx[name] + 1].record()
 
     try:
-        runner = GraphRunner(lambda: blk.run_kernels(hook=hook))
-        per_kernel_events = True
-    except Exception as e:  # graph event nodes unsupported: time the graph without them
+        prof_runner = GraphRunner(lambda: blk.run_kernels(hook=hook))
+    except Exception as e:  # graph event nodes unsupported: per-kernel times from eager launches
         print(f"[bench] per-kernel events in graph unavailable ({e}); timing kernels eagerly", file=sys.stderr)
-        runner = GraphRunner(lambda: blk.run_kernels())
-        per_kernel_events = False
+        prof_runner = None
 
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream()
@@ -213,7 +216,6 @@ def bench_block(args, rank, world, device):
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    kernel_ms = {k: [] for k in KERNEL_ORDER}
     with ClockSampler(torch.cuda.current_device()) as clk:
         _barrier(world)
         torch.cuda.synchronize()
@@ -222,16 +224,22 @@ def bench_block(args, rank, world, device):
             starts[i].record(stream)
             runner.replay()
             ends[i].record(stream)
-            if per_kernel_events:
-                ends[i].synchronize()
-                for k, name in enumerate(KERNEL_ORDER):
-                    kernel_ms[name].append(evs[k].elapsed_time(evs[k + 1]))
         torch.cuda.synchronize()
         _barrier(world)
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = _max_over_ranks(sum(step_ms), world)
 
-    if not per_kernel_events:
+    kernel_ms = {k: [] for k in KERNEL_ORDER}
+    if prof_runner is not None:
+        for i in range(args.steps + 1):
+            flush.zero_()
+            prof_runner.replay()
+            torch.cuda.synchronize()
+            if i > 0:
+                for k, name in enumerate(KERNEL_ORDER):
+                    kernel_ms[name].append(evs[k].elapsed_time(evs[k + 1]))
+        prof_runner.release()
+    else:
         eager = {k: [] for k in KERNEL_ORDER}
         cur = {}
 
@@ -278,7 +286,7 @@ def bench_block(args, rank, world, device):
         "kernel_ms": mean_k, "dominant": dom, "dominant_flops": flops[dom],
         "launches_per_step": len(KERNEL_ORDER),
         "clocks": clk.summary(),
-        "per_kernel_events": per_kernel_events,
+        "per_kernel_events": prof_runner is not None,
     }
 
 
@@ -334,7 +342,8 @@ def main():
                        "global_batch": 8 * world, "seq_len": 512,
                        "parallelism": f"batch-sharded replicas x{world} (no collective)",
                        "l2": "256 MB flush write between timed steps",
-                       "graph": "7 kernels in one CUDA graph"},
+                       "graph": "7 kernels in one CUDA graph (programmatic dependent launch)",
+                       "kernel_timing": "per-kernel CUDA events from an instrumented replay of the same graph"},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": r["h2d"] * world,
                     "d2h_bytes_per_step": r["d2h"] * world},
             "gpu_launches": r["launches_per_step"] * args.steps,

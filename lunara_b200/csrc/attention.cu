@@ -134,6 +134,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();
+  pdl_launch_dependents();
   // Each role adjusts its register budget at the top of its own branch, so the
   // compiler allocates every branch with that branch's budget.
   if (warp == 8) {
@@ -498,8 +500,7 @@ cudaError_t run_tc(const AttnArgs& a, cudaStream_t s) {
   unsigned int* err = device_error_word();
   if (err == nullptr) return cudaErrorInvalidDevice;
   const dim3 grid(static_cast<unsigned>(p.n_qblocks), static_cast<unsigned>(a.H), static_cast<unsigned>(a.B));
-  kern<<<grid, kAttnThreads, kAttnSmem, s>>>(mq, mk, mv, p, err);
-  return cudaGetLastError();
+  return launch_pdl(kern, grid, dim3(kAttnThreads), static_cast<size_t>(kAttnSmem), s, mq, mk, mv, p, err);
 }
 
 }  // namespace

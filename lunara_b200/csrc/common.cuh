@@ -49,6 +49,17 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ------------------------------------------- programmatic dependent launch --
+// Kernels are launched with programmatic stream serialization: a kernel may be
+// scheduled while its predecessor in the stream is still finishing, runs its
+// prologue (barrier init, TMEM allocation, descriptor prefetch), and waits in
+// pdl_wait() until the predecessor's writes are visible before touching any
+// global input or output. pdl_launch_dependents() lets the successor be
+// scheduled once every CTA of this grid has started. Both are no-ops for a
+// launch without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- mbarrier --
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");

@@ -52,6 +52,8 @@ constexpr int kThreads = 256;
 
 template <typename T, int ACT>
 __global__ void __launch_bounds__(kThreads) unary_kernel(const T* __restrict__ X, T* __restrict__ Y, int64_t n) {
+  pdl_wait();
+  pdl_launch_dependents();
   constexpr int EPV = kEpv<T>;
   const int64_t nvec = n / EPV;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
@@ -96,6 +98,8 @@ __device__ __forceinline__ float bin(float a, float b) {
 template <typename T, int OP>
 __global__ void __launch_bounds__(kThreads) binary_kernel(const T* __restrict__ X, const T* __restrict__ Yin,
                                                           T* __restrict__ Out, int64_t n, int vec) {
+  pdl_wait();
+  pdl_launch_dependents();
   constexpr int EPV = kEpv<T>;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
@@ -123,6 +127,8 @@ __global__ void __launch_bounds__(kThreads) binary_kernel(const T* __restrict__ 
 template <typename T, int ACT, typename IdxT>
 __global__ void __launch_bounds__(kThreads) bias_act_kernel(const T* __restrict__ X, const T* __restrict__ bias,
                                                             T* __restrict__ Y, IdxT nvec, IdxT vec_per_row) {
+  pdl_wait();
+  pdl_launch_dependents();
   constexpr int EPV = kEpv<T>;
   const IdxT stride = static_cast<IdxT>(gridDim.x) * kThreads;
   const uint4* xv = reinterpret_cast<const uint4*>(X);
@@ -178,9 +184,10 @@ cudaError_t unary_t(int act, const void* X, void* Y, int64_t n, cudaStream_t s) 
   T* y = static_cast<T*>(Y);
   const bool vec = al16(X) && al16(Y);
   const unsigned grid = grid_for(vec ? n / kEpv<T> + 1 : n, 2);
+  cudaError_t e = cudaSuccess;
 #define UN_CASE(A)                                                                           \
   case A:                                                                                    \
-    if (vec) unary_kernel<T, A><<<grid, kThreads, 0, s>>>(x, y, n);                          \
+    if (vec) e = launch_pdl(unary_kernel<T, A>, dim3(grid), dim3(kThreads), 0, s, x, y, n);  \
     else unary_scalar_kernel<T, A><<<grid, kThreads, 0, s>>>(x, y, n);                       \
     break;
   switch (act) {
@@ -189,6 +196,7 @@ cudaError_t unary_t(int act, const void* X, void* Y, int64_t n, cudaStream_t s) 
     default: return cudaErrorInvalidValue;
   }
 #undef UN_CASE
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -199,9 +207,9 @@ cudaError_t binary_t(int op, const void* X, const void* Yin, void* Out, int64_t 
   const T* x = static_cast<const T*>(X);
   const T* yi = static_cast<const T*>(Yin);
   T* o = static_cast<T*>(Out);
-  if (op == LUNARA_BIN_ADD) binary_kernel<T, LUNARA_BIN_ADD><<<grid, kThreads, 0, s>>>(x, yi, o, n, vec);
-  else binary_kernel<T, LUNARA_BIN_MUL><<<grid, kThreads, 0, s>>>(x, yi, o, n, vec);
-  return cudaGetLastError();
+  if (op == LUNARA_BIN_ADD)
+    return launch_pdl(binary_kernel<T, LUNARA_BIN_ADD>, dim3(grid), dim3(kThreads), 0, s, x, yi, o, n, vec);
+  return launch_pdl(binary_kernel<T, LUNARA_BIN_MUL>, dim3(grid), dim3(kThreads), 0, s, x, yi, o, n, vec);
 }
 
 template <typename T, int ACT>
@@ -212,11 +220,10 @@ cudaError_t bias_act_tt(const T* x, const T* b, T* y, int64_t rows, int64_t cols
     const int64_t nvec = n / EPV, vpr = cols / EPV;
     const unsigned grid = grid_for(nvec, 2);
     if (nvec + 2 * int64_t{grid} * kThreads < (int64_t{1} << 31))
-      bias_act_kernel<T, ACT, uint32_t><<<grid, kThreads, 0, s>>>(x, b, y, static_cast<uint32_t>(nvec),
-                                                                  static_cast<uint32_t>(vpr));
-    else
-      bias_act_kernel<T, ACT, uint64_t><<<grid, kThreads, 0, s>>>(x, b, y, static_cast<uint64_t>(nvec),
-                                                                  static_cast<uint64_t>(vpr));
+      return launch_pdl(bias_act_kernel<T, ACT, uint32_t>, dim3(grid), dim3(kThreads), 0, s, x, b, y,
+                        static_cast<uint32_t>(nvec), static_cast<uint32_t>(vpr));
+    return launch_pdl(bias_act_kernel<T, ACT, uint64_t>, dim3(grid), dim3(kThreads), 0, s, x, b, y,
+                      static_cast<uint64_t>(nvec), static_cast<uint64_t>(vpr));
   } else {
     bias_act_scalar_kernel<T, ACT><<<grid_for(n, 1), kThreads, 0, s>>>(x, b, y, n, cols);
   }

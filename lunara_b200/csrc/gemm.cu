@@ -341,6 +341,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();
+  pdl_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -544,6 +546,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   cluster_sync();   // barriers of both CTAs initialised before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();
+  pdl_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -832,10 +836,8 @@ cudaError_t run_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& 
   if (grid > tiles) grid = tiles;
   unsigned int* err = device_error_word();
   if (err == nullptr) return cudaErrorInvalidDevice;
-  kern<<<static_cast<unsigned>(grid), kGemmThreads, smem, s>>>(ma, mb, mc, ep, static_cast<int>(g.M),
-                                                               static_cast<int>(g.N), static_cast<int>(g.K),
-                                                               stages, err);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(kGemmThreads), static_cast<size_t>(smem), s, ma, mb,
+                    mc, ep, static_cast<int>(g.M), static_cast<int>(g.N), static_cast<int>(g.K), stages, err);
 }
 
 template <typename T, int BN, bool B_KMAJOR, int EPI>
@@ -876,9 +878,9 @@ cudaError_t run_tc2(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap&
   if (clusters < 1) clusters = 1;
   unsigned int* err = device_error_word();
   if (err == nullptr) return cudaErrorInvalidDevice;
-  kern<<<static_cast<unsigned>(2 * clusters), kGemmThreads, smem, s>>>(
-      ma, mb, mc, ep, static_cast<int>(g.M), static_cast<int>(g.N), static_cast<int>(g.K), stages, err);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(static_cast<unsigned>(2 * clusters)), dim3(kGemmThreads), static_cast<size_t>(smem), s,
+                    ma, mb, mc, ep, static_cast<int>(g.M), static_cast<int>(g.N), static_cast<int>(g.K), stages,
+                    err);
 }
 
 template <typename T, bool B_KMAJOR, int EPI>

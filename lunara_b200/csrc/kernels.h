@@ -4,11 +4,32 @@
 #pragma once
 
 #include <cuda_runtime.h>
+
 #include <cstdint>
+#include <utility>
 
 namespace lunara {
 
 int device_num_sms();
+
+// Launch with programmatic stream serialization: the kernel may be scheduled
+// before its predecessor in the stream has finished and waits for it in
+// pdl_wait() (common.cuh). Used for every kernel of the hot path.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // Device address of the library's error word on the current device (cached
 // per device); nullptr when the symbol cannot be resolved.

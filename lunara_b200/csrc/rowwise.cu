@@ -82,6 +82,8 @@ __global__ void __launch_bounds__(kRowThreads) layernorm_warp_kernel(const T* __
                                                                      const T* __restrict__ gamma,
                                                                      const T* __restrict__ beta, T* __restrict__ Y,
                                                                      int64_t M, int N, float eps) {
+  pdl_wait();
+  pdl_launch_dependents();
   constexpr int EPV = VecTraits<T>::kElems;
   const int nv = N / EPV;
   const int lane = threadIdx.x & 31;
@@ -185,6 +187,8 @@ constexpr float kLog2e = 1.4426950408889634f;
 template <typename T, int VPL>
 __global__ void __launch_bounds__(kRowThreads) softmax_warp_kernel(const T* __restrict__ X, T* __restrict__ Y,
                                                                    int64_t M, int N) {
+  pdl_wait();
+  pdl_launch_dependents();
   constexpr int EPV = VecTraits<T>::kElems;
   const int nv = N / EPV;
   const int lane = threadIdx.x & 31;
@@ -271,14 +275,16 @@ cudaError_t layernorm_t(const void* X, const void* g, const void* b, void* Y, in
   if (vpl > 0) {
     const dim3 grid(static_cast<unsigned>(ceil_div64(M, kRowThreads / 32)));
     const int n = static_cast<int>(N);
+    cudaError_t e = cudaSuccess;
     switch (vpl) {
 #define LN_CASE(V)                                                                               \
   case V:                                                                                        \
-    layernorm_warp_kernel<T, V><<<grid, kRowThreads, 0, s>>>(x, gg, bb, y, M, n, eps);          \
+    e = launch_pdl(layernorm_warp_kernel<T, V>, grid, dim3(kRowThreads), 0, s, x, gg, bb, y, M, n, eps); \
     break;
       LN_CASE(1) LN_CASE(2) LN_CASE(3) LN_CASE(4) LN_CASE(6) LN_CASE(8) LN_CASE(12) LN_CASE(16)
 #undef LN_CASE
     }
+    return e;
   } else {
     layernorm_block_kernel<T><<<static_cast<unsigned>(M), kRowThreads, 0, s>>>(x, gg, bb, y, N, eps);
   }
@@ -295,14 +301,16 @@ cudaError_t softmax_t(const void* X, void* Y, int64_t M, int64_t N, cudaStream_t
   if (vpl > 0) {
     const dim3 grid(static_cast<unsigned>(ceil_div64(M, kRowThreads / 32)));
     const int n = static_cast<int>(N);
+    cudaError_t e = cudaSuccess;
     switch (vpl) {
 #define SM_CASE(V)                                                                 \
   case V:                                                                          \
-    softmax_warp_kernel<T, V><<<grid, kRowThreads, 0, s>>>(x, y, M, n);           \
+    e = launch_pdl(softmax_warp_kernel<T, V>, grid, dim3(kRowThreads), 0, s, x, y, M, n); \
     break;
       SM_CASE(1) SM_CASE(2) SM_CASE(3) SM_CASE(4) SM_CASE(6) SM_CASE(8) SM_CASE(12) SM_CASE(16)
 #undef SM_CASE
     }
+    return e;
   } else {
     softmax_block_kernel<T><<<static_cast<unsigned>(M), kRowThreads, 0, s>>>(x, y, N);
   }
