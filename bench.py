@@ -69,14 +69,24 @@ def _traffic_from_profiles(kernel: str, workload: str):
 class ClockSampler:
     """nvidia-smi clock / throttle-reason sampling during the timed region."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    INTERVAL_MS = 20
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
         self.path = None
+        self.window = None
+
+    def mark(self, start: bool):
+        """Host wall-clock bounds of the timed region (samples outside it are dropped)."""
+        now = datetime.datetime.now()
+        if start:
+            self.window = [now, None]
+        elif self.window is not None:
+            self.window[1] = now
 
     def __enter__(self):
         try:
@@ -84,7 +94,7 @@ class ClockSampler:
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+                 "-lms", str(self.INTERVAL_MS), "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
             time.sleep(0.3)
         except (FileNotFoundError, OSError):
             self.proc = None
@@ -104,18 +114,32 @@ class ClockSampler:
         rows = []
         for line in Path(self.path).read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
+            if len(parts) < 10:
+                continue
+            try:
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
+            except ValueError:
+                continue
+            rows.append((ts, parts[1:]))
         os.unlink(self.path)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        inside = rows
+        if self.window is not None and self.window[1] is not None:
+            lo, hi = self.window
+            inside = [r for r in rows if lo <= r[0] <= hi]
+            if not inside:   # timed region shorter than the sampling interval: nearest sample after its start
+                after = [r for r in rows if r[0] >= lo] or rows[-1:]
+                inside = after[:1]
+        rows = [r[1] for r in inside]
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        busy = [s for s in sm if s > 0.5 * (max(mx) if mx else 1)] or sm
-        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows),
+                "window_ms": round((self.window[1] - self.window[0]).total_seconds() * 1e3, 1)
+                if self.window and self.window[1] else None}
 
 
 # ─────────────────────────────────────────────────────────── reference arm ──
@@ -136,7 +160,9 @@ def cpu_block_sample(budget_s: float, steps: int = 0, warmup: int = 1, batch: in
         times.append(time.perf_counter() - t0)
         if steps and len(times) >= steps:
             break
-        if not steps and (time.perf_counter() - t_start > budget_s or len(times) >= 50):
+        if budget_s and time.perf_counter() - t_start > budget_s:
+            break
+        if not steps and len(times) >= 50:
             break
     tokens = batch * seq
     return {"value": tokens * len(times) / sum(times), "unit": "tokens/s", "cores": threads,
@@ -147,7 +173,9 @@ def cpu_block_sample(budget_s: float, steps: int = 0, warmup: int = 1, batch: in
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    cb = cpu_block_sample(budget_s=0, steps=args.steps, warmup=args.warmup)
+    # K steps of one block forward each, stopped after 90 s of host time so that
+    # a long --steps run still ends within minutes (the sample says how many ran).
+    cb = cpu_block_sample(budget_s=90.0, steps=args.steps, warmup=min(args.warmup, 3))
     line = {"impl": "reference", "metric": TOKENS_METRIC, "value": cb["value"], "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 4096 / cb["value"] * 1e3, "higher_is_better": True, "scaling": "weak",
@@ -219,12 +247,14 @@ def bench_block(args, rank, world, device):
     with ClockSampler(torch.cuda.current_device()) as clk:
         _barrier(world)
         torch.cuda.synchronize()
+        clk.mark(True)
         for i in range(args.steps):
             flush.zero_()
             starts[i].record(stream)
             runner.replay()
             ends[i].record(stream)
         torch.cuda.synchronize()
+        clk.mark(False)
         _barrier(world)
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = _max_over_ranks(sum(step_ms), world)
@@ -293,8 +323,8 @@ def bench_block(args, rank, world, device):
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["lunara", "reference"], default="lunara")
     ap.add_argument("--workload", default="block",
                     choices=["block", "stack", "gemm", "attention", "attention_causal", "layernorm", "bias_gelu"])

@@ -66,7 +66,8 @@ typedef enum lunara_b_layout {
 /* Optional tile request for the GEMM (the sm_100a counterpart of TileConfig,
  * triton_emitter.py:44-56). Zero fields mean "choose automatically".
  *   block_n : tcgen05 MMA N: 64, 128, 192 or 256 for 128-row tiles of one
- *             CTA; 128 or 256 for 256-row tiles of a CTA pair
+ *             CTA; 128, 192 (B as [N,K] only) or 256 for 256-row tiles of a
+ *             CTA pair
  *   stages  : shared-memory pipeline depth (2..8)
  *   num_ctas: persistent grid size (0 = every SM / SM pair)
  *   cta_pair: 1 = single-CTA tiles, 2 = CTA-pair tiles (cta_group::2),

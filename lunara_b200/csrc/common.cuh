@@ -392,9 +392,12 @@ __device__ __forceinline__ float apply_act(float v, int act) {
     case LUNARA_ACT_GELU_ERF:
       return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
     case LUNARA_ACT_GELU_TANH: {
-      // Hendrycks & Gimpel tanh form: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
-      const float u = 0.7978845608028654f * fmaf(0.044715f * v, v * v, v);
-      return 0.5f * v * (1.0f + tanh_approx(u));
+      // Hendrycks & Gimpel tanh form: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))),
+      // evaluated as u = x (c0 + c1 x^2), y = h + h tanh(u) with h = x / 2:
+      // five FMA-pipe operations and one tanh.
+      const float u = v * fmaf(0.0356774081363001f, v * v, 0.7978845608028654f);
+      const float h = 0.5f * v;
+      return fmaf(h, tanh_approx(u), h);
     }
     case LUNARA_ACT_SIGMOID:
       return 1.0f / (1.0f + __expf(-v));

@@ -110,6 +110,18 @@ __device__ __forceinline__ void load_residual(ResChunk& rc, int row, int col0, c
   }
 }
 
+// Pulls this lane's residual row segment [c0, c0 + count) into L2 while the
+// tile's main loop is still running, so that the epilogue's residual loads
+// (issued only once the accumulator is complete) hit L2 instead of HBM.
+template <typename T>
+__device__ __forceinline__ void prefetch_residual(int row, int c0, int count, const EpiParams& ep) {
+  if (ep.residual == nullptr || row >= ep.M) return;
+  const char* p = reinterpret_cast<const char*>(static_cast<const T*>(ep.residual) +
+                                                static_cast<int64_t>(row) * ep.ldr + c0);
+  const int bytes = min(count, ep.N - c0) * static_cast<int>(sizeof(T));
+  for (int off = 0; off < bytes; off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + off));
+}
+
 // Epilogue for 32 consecutive accumulator columns of one row: + bias (staged
 // in shared memory as fp32), activation, + residual, one rounding, store.
 template <typename T, int EPI>
@@ -240,16 +252,16 @@ __device__ __forceinline__ void epilogue_out(const uint32_t (&acc)[32], int row,
 
 // The epilogue of one accumulator tile for one warp: `kHalf` columns starting at
 // c0 for the 32 rows starting at row0_warp (this lane's row = row0_warp + lane),
-// read from TMEM at t_row one 32-column chunk ahead of their use.
+// read from TMEM at t_row one 32-column chunk ahead of their use. res[0] holds
+// the residual of the first chunk, loaded by the caller before the accumulator
+// was ready.
 template <typename T, int BN, int EPI>
 __device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row0_warp, int c0, const float* sb,
                                               const EpiParams& ep, const CUtensorMap* tma_c, uint8_t* s_stage,
-                                              int lane) {
+                                              int lane, ResChunk (&res)[2]) {
   constexpr int kHalf = BN / 2;
   constexpr int kChunks = kHalf / 32;
   const int row = row0_warp + lane;
-  ResChunk res[2];
-  load_residual<T>(res[0], row, c0, ep);
   // Chunks are processed in pairs (two register buffers, compile-time
   // indices); the loop itself is not unrolled to keep the code small.
   uint32_t v[2][32];
@@ -443,13 +455,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int m0 = (tile % m_tiles) * BM;
       const int n0 = (tile / m_tiles) * BN;
       const int c0 = n0 + half * kHalf;
+      ResChunk res[2];
+      prefetch_residual<T>(m0 + quarter * 32 + lane, c0, kHalf, ep);
+      load_residual<T>(res[0], m0 + quarter * 32 + lane, c0, ep);
       stage_bias<T>(sb, c0, kHalf, ep, lane);
       __syncwarp();
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, err, kErrGemmEpilogue)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * ACC_STRIDE +
                              half * kHalf;
-      epilogue_tile<T, BN, EPI>(t_row, m0 + quarter * 32, c0, sb, ep, &tma_c, s_stage, lane);
+      epilogue_tile<T, BN, EPI>(t_row, m0 + quarter * 32, c0, sb, ep, &tma_c, s_stage, lane, res);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
@@ -493,6 +508,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
                     const __grid_constant__ CUtensorMap tma_c, const EpiParams ep, const int M, const int N, const int K, const int STAGES,
                     unsigned int* err) {
   constexpr int BH = BN / 2;                     // B rows (K-major) / columns (MN-major) per CTA
+  static_assert(B_KMAJOR || BH % 64 == 0, "MN-major B halves are loaded as whole 64-column boxes");
   constexpr uint32_t A_BYTES = BM * BK * 2;
   constexpr uint32_t B_BYTES = BH * BK * 2;
   constexpr uint32_t TMEM_COLS = tmem_cols_for(BN);
@@ -656,13 +672,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       const int m0 = (tile % m_tiles) * 2 * BM + static_cast<int>(rank) * BM;
       const int n0 = (tile / m_tiles) * BN;
       const int c0 = n0 + half * kHalf;
+      ResChunk res[2];
+      prefetch_residual<T>(m0 + quarter * 32 + lane, c0, kHalf, ep);
+      load_residual<T>(res[0], m0 + quarter * 32 + lane, c0, ep);
       stage_bias<T>(sb, c0, kHalf, ep, lane);
       __syncwarp();
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, err, kErrGemmEpilogue)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * ACC_STRIDE +
                              half * kHalf;
-      epilogue_tile<T, BN, EPI>(t_row, m0 + quarter * 32, c0, sb, ep, &tma_c, s_stage, lane);
+      epilogue_tile<T, BN, EPI>(t_row, m0 + quarter * 32, c0, sb, ep, &tma_c, s_stage, lane, res);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_tempty + acc * 8);
@@ -801,15 +820,16 @@ double gemm_cost(int64_t M, int64_t N, int64_t K, GemmPlan p, int sms) {
   return static_cast<double>(rounds) * (static_cast<double>(ceil_div64(K, BK)) * per_kb + 800.0);
 }
 
-GemmPlan choose_plan(int64_t M, int64_t N, int64_t K, int sms, int block_n, int cta_pair) {
-  static const GemmPlan kChoices[] = {{256, true}, {128, true}, {256, false}, {192, false}, {128, false},
-                                      {64, false}};
+GemmPlan choose_plan(int64_t M, int64_t N, int64_t K, int sms, int block_n, int cta_pair, bool b_kmajor) {
+  static const GemmPlan kChoices[] = {{256, true}, {192, true}, {128, true}, {256, false}, {192, false},
+                                      {128, false}, {64, false}};
   GemmPlan best{256, true};
   double best_cost = 1e300;
   for (const GemmPlan& c : kChoices) {
     if (block_n != 0 && c.block_n != block_n) continue;
     if (cta_pair == 1 && c.pair) continue;
     if (cta_pair == 2 && !c.pair) continue;
+    if (c.pair && c.block_n == 192 && !b_kmajor) continue;   // MN-major halves must be whole 64-column boxes
     const double cost = gemm_cost(M, N, K, c, sms);
     if (cost < best_cost * 0.999) {
       best_cost = cost;
@@ -887,8 +907,11 @@ template <typename T, bool B_KMAJOR, int EPI>
 cudaError_t dispatch_epi(const GemmArgs& g, GemmPlan plan, const CUtensorMap& ma, const CUtensorMap& mb,
                          const CUtensorMap& mc, const EpiParams& ep, cudaStream_t s) {
   if (plan.pair) {
-    return plan.block_n == 128 ? run_tc2<T, 128, B_KMAJOR, EPI>(g, ma, mb, mc, ep, s)
-                               : run_tc2<T, 256, B_KMAJOR, EPI>(g, ma, mb, mc, ep, s);
+    if (plan.block_n == 128) return run_tc2<T, 128, B_KMAJOR, EPI>(g, ma, mb, mc, ep, s);
+    if constexpr (B_KMAJOR) {
+      if (plan.block_n == 192) return run_tc2<T, 192, B_KMAJOR, EPI>(g, ma, mb, mc, ep, s);
+    }
+    return run_tc2<T, 256, B_KMAJOR, EPI>(g, ma, mb, mc, ep, s);
   }
   switch (plan.block_n) {
     case 64: return run_tc<T, 64, B_KMAJOR, EPI>(g, ma, mb, mc, ep, s);
@@ -937,9 +960,9 @@ cudaError_t launch_gemm_tcgen05(const GemmArgs& g, cudaStream_t stream) {
   int bn = g.block_n;
   if (bn != 64 && bn != 128 && bn != 192 && bn != 256) bn = 0;
   int pair = g.cta_pair;
-  if (bn == 64 || bn == 192) pair = 1;
-  const GemmPlan plan = choose_plan(g.M, g.N, g.K, device_num_sms(), bn, pair);
   const bool kmajor = g.b_layout == LUNARA_B_NK;
+  if (bn == 64 || (bn == 192 && !kmajor)) pair = 1;
+  const GemmPlan plan = choose_plan(g.M, g.N, g.K, device_num_sms(), bn, pair, kmajor);
   if (g.dtype == LUNARA_BF16)
     return kmajor ? dispatch_plan<__nv_bfloat16, true>(g, plan, stream)
                   : dispatch_plan<__nv_bfloat16, false>(g, plan, stream);

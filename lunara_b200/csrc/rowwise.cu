@@ -112,8 +112,8 @@ __global__ void __launch_bounds__(kRowThreads) layernorm_warp_kernel(const T* __
     if (lane + i * 32 < nv) {
 #pragma unroll
       for (int e = 0; e < EPV; ++e) {
-        const float d = v[i][e] - mean;
-        sq = fmaf(d, d, sq);
+        v[i][e] -= mean;
+        sq = fmaf(v[i][e], v[i][e], sq);
       }
     }
   }
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kRowThreads) layernorm_warp_kernel(const T* __
       unpack_vec<T>(__ldg(gv + vi), g);
       unpack_vec<T>(__ldg(bv + vi), b);
 #pragma unroll
-      for (int e = 0; e < EPV; ++e) o[e] = fmaf((v[i][e] - mean) * rstd, g[e], b[e]);
+      for (int e = 0; e < EPV; ++e) o[e] = fmaf(v[i][e] * rstd, g[e], b[e]);
       yr[vi] = pack_vec<T>(o);
     }
   }

@@ -42,9 +42,10 @@ def test_gemm_tile_widths(dtype, layout, bn):
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("layout", ["kn", "nk"])
-@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("bn", [128, 192, 256])
 def test_gemm_cta_pair_tiles(dtype, layout, bn):
-    """256-row tiles computed by a CTA pair (cta_group::2 MMA), several tiles per pair."""
+    """256-row tiles computed by a CTA pair (cta_group::2 MMA), several tiles per pair.
+    (N=192 pair tiles take B as [N,K]; with B as [K,N] the request runs on single-CTA tiles.)"""
     M, N, K = 1024, 768, 320
     a, b, bias, res = _mk(M, N, K, dtype, bn + 1, layout, scale=0.5)
     ops = _ops()
