@@ -14,8 +14,10 @@ the launching stream, with a 256 MB L2-flush write between steps (outside the
 events); a barrier and torch.cuda.synchronize() on both sides of the K steps;
 the max over ranks is reported. Multi-GPU (torchrun, one rank per GPU, NCCL) is
 batch sharding with no collective on the data path: every rank runs its own
-batch-8 block (weak scaling). `e2e` repeats the step through the host-facing
-API (pinned host input -> device, block, device -> pinned host output).
+batch-8 block (weak scaling). `e2e` runs the step as a serving loop does: the
+input copied from pinned host memory, the block, the output copied back to
+pinned host memory, every step, with the copies of neighbouring steps
+overlapping the kernels on their own streams (two buffer pairs).
 `--impl reference` times the reference's CPU path (torch eager fp32 on the host
 cores, the oracle) on the same workload.
 """
@@ -55,10 +57,12 @@ def _peaks():
 
 
 def _traffic_from_profiles(kernel: str, workload: str):
-    """DRAM bytes per launch recorded in profiles/<kernel>_<workload>.md (line 'dram_bytes_per_launch: N')."""
-    for f in sorted((ROOT / "profiles").glob(f"{kernel}_{workload}*.md")):
+    """DRAM bytes per launch of a kernel, from the ncu summary profiles/<workload>*.md
+    (line 'dram_bytes_per_launch[<kernel>]: N')."""
+    key = f"dram_bytes_per_launch[{kernel}]:"
+    for f in sorted((ROOT / "profiles").glob(f"{workload}*.md")):
         for line in f.read_text().splitlines():
-            if line.strip().startswith("dram_bytes_per_launch:"):
+            if line.strip().startswith(key):
                 try:
                     return float(line.split(":", 1)[1].strip().split()[0])
                 except ValueError:
@@ -214,26 +218,14 @@ def bench_block(args, rank, world, device):
     flops = block_flops(batch * seq, seq)
 
     # Timed graph: the seven kernels alone (adjacent kernel nodes keep their
-    # programmatic-launch overlap). A second copy of the graph with an event
-    # between kernels (external events) gives per-kernel durations; it is
-    # replayed in its own loop after the timed one, since event nodes between
-    # kernels serialise them.
+    # programmatic-launch overlap).
     runner = GraphRunner(lambda: blk.run_kernels())
-    n_ev = len(KERNEL_ORDER) + 1
-    evs = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_ev)]
-    idx = {name: i for i, name in enumerate(KERNEL_ORDER)}
-
-    def hook(name, where):
-        if where == "begin" and name == KERNEL_ORDER[0]:
-            evs[0].record()
-        elif where == "end":
-            evs[idx[name] + 1].record()
-
-    try:
-        prof_runner = GraphRunner(lambda: blk.run_kernels(hook=hook))
-    except Exception as e:  # graph event nodes unsupported: per-kernel times from eager launches
-        print(f"[bench] per-kernel events in graph unavailable ({e}); timing kernels eagerly", file=sys.stderr)
-        prof_runner = None
+    # Per-kernel durations: one graph per kernel holding REPS back-to-back
+    # launches of it on the block's own buffers (every launch is idempotent),
+    # timed with events around the replay, replayed after the timed loop.
+    reps = 20
+    fns = blk.kernel_fns()
+    kernel_runners = {name: GraphRunner(lambda f=f: [f() for _ in range(reps)]) for name, f in fns.items()}
 
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream()
@@ -260,63 +252,79 @@ def bench_block(args, rank, world, device):
     total_ms = _max_over_ranks(sum(step_ms), world)
 
     kernel_ms = {k: [] for k in KERNEL_ORDER}
-    if prof_runner is not None:
-        for i in range(args.steps + 1):
+    for name, kr in kernel_runners.items():
+        for i in range(6):
             flush.zero_()
-            prof_runner.replay()
-            torch.cuda.synchronize()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            kr.replay()
+            s1.record(stream)
+            s1.synchronize()
             if i > 0:
-                for k, name in enumerate(KERNEL_ORDER):
-                    kernel_ms[name].append(evs[k].elapsed_time(evs[k + 1]))
-        prof_runner.release()
-    else:
-        eager = {k: [] for k in KERNEL_ORDER}
-        cur = {}
+                kernel_ms[name].append(s0.elapsed_time(s1) / reps)
+        kr.release()
 
-        def ehook(name, where):
-            if where == "begin":
-                cur[name] = torch.cuda.Event(enable_timing=True)
-                cur[name].record()
-            else:
-                e = torch.cuda.Event(enable_timing=True)
-                e.record()
-                eager[name].append((cur[name], e))
-        for _ in range(args.steps):
-            flush.zero_()
-            blk.run_kernels(hook=ehook)
-        torch.cuda.synchronize()
-        kernel_ms = {k: [a.elapsed_time(b) for a, b in v] for k, v in eager.items()}
-
-    # End to end through host buffers: pinned input -> device, block, device -> pinned output.
+    # End to end through host buffers, as a serving loop runs it: every step
+    # copies its input from pinned host memory (H2D stream), runs the block
+    # (compute stream, with the L2 flush) and copies its output back to pinned
+    # host memory (D2H stream). Two input/output buffer pairs let step i+1's
+    # H2D and step i-1's D2H overlap step i's kernels; events order the reuse
+    # of each buffer. Whole-loop time / steps.
     x_host = x.half().view(batch * seq, 768).pin_memory()
-    y_host = torch.empty(batch * seq, 768, dtype=torch.float16).pin_memory()
-    e2e_ms = []
-    for i in range(args.steps + args.warmup):
-        flush.zero_()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        blk.x.copy_(x_host, non_blocking=True)
-        out = runner.replay()
-        y_host.copy_(out, non_blocking=True)
-        e.record(stream)
-        e.synchronize()
-        if i >= args.warmup:
-            e2e_ms.append(s.elapsed_time(e))
-    e2e_total = _max_over_ranks(sum(e2e_ms), world)
-    runner.release()
+    y_hosts = [torch.empty(batch * seq, 768, dtype=torch.float16).pin_memory() for _ in range(2)]
+    xb = [blk.x, torch.empty_like(blk.x)]
+    yb = [blk.y, torch.empty_like(blk.y)]
+    e2e_runners = [runner, GraphRunner(lambda: blk.run_kernels(x=xb[1], out=yb[1]))]
+    h2d_s, d2h_s = torch.cuda.Stream(), torch.cuda.Stream()
 
-    mean_k = {k: statistics.mean(v) for k, v in kernel_ms.items() if v}
+    def e2e_loop(n):
+        ev = lambda: torch.cuda.Event()  # noqa: E731
+        h2d_done, comp_done, d2h_done = [ev(), ev()], [ev(), ev()], [ev(), ev()]
+        for i in range(n):
+            k = i % 2
+            if i >= 2:
+                h2d_s.wait_event(comp_done[k])        # step i-2 has finished reading xb[k]
+            with torch.cuda.stream(h2d_s):
+                xb[k].copy_(x_host, non_blocking=True)
+                h2d_done[k].record(h2d_s)
+            stream.wait_event(h2d_done[k])
+            if i >= 2:
+                stream.wait_event(d2h_done[k])        # step i-2's output has left yb[k]
+            flush.zero_()
+            e2e_runners[k].replay()
+            comp_done[k].record(stream)
+            d2h_s.wait_event(comp_done[k])
+            with torch.cuda.stream(d2h_s):
+                y_hosts[k].copy_(yb[k], non_blocking=True)
+                d2h_done[k].record(d2h_s)
+        stream.wait_stream(d2h_s)
+        stream.wait_stream(h2d_s)
+
+    e2e_loop(max(args.warmup, 2))
+    torch.cuda.synchronize()
+    _barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    e2e_loop(args.steps)
+    e1.record(stream)
+    e1.synchronize()
+    _barrier(world)
+    e2e_total = _max_over_ranks(e0.elapsed_time(e1), world)
+    assert torch.equal(y_hosts[(args.steps - 1) % 2], yb[(args.steps - 1) % 2].cpu()), "e2e output mismatch"
+    for r_ in e2e_runners:
+        r_.release()
+
+    mean_k = {k: statistics.median(v) for k, v in kernel_ms.items() if v}
     dom = max(mean_k, key=mean_k.get)
     tokens = batch * seq
     return {
         "tokens_per_step": tokens * world,
         "total_ms": total_ms,
         "e2e_total_ms": e2e_total,
-        "h2d": x_host.numel() * 2, "d2h": y_host.numel() * 2,
+        "h2d": x_host.numel() * 2, "d2h": y_hosts[0].numel() * 2,
         "kernel_ms": mean_k, "dominant": dom, "dominant_flops": flops[dom],
         "launches_per_step": len(KERNEL_ORDER),
         "clocks": clk.summary(),
-        "per_kernel_events": prof_runner is not None,
     }
 
 
@@ -373,7 +381,8 @@ def main():
                        "parallelism": f"batch-sharded replicas x{world} (no collective)",
                        "l2": "256 MB flush write between timed steps",
                        "graph": "7 kernels in one CUDA graph (programmatic dependent launch)",
-                       "kernel_timing": "per-kernel CUDA events from an instrumented replay of the same graph"},
+                       "kernel_timing": "per kernel: CUDA events around a graph of 20 back-to-back launches "
+                                        "on the block's buffers, / 20 (median of 5)"},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": r["h2d"] * world,
                     "d2h_bytes_per_step": r["d2h"] * world},
             "gpu_launches": r["launches_per_step"] * args.steps,

@@ -47,10 +47,20 @@ constexpr int kProducerRegs = 56;
 constexpr int kSoftmaxRegs = 224;
 static_assert(128 * kProducerRegs + 256 * kSoftmaxRegs <= kAttnThreads * kLaunchRegs, "register split");
 constexpr float kRescaleLog2 = 8.0f;
-// Exponential pairs evaluated on the FMA pipe instead of MUFU (one pair in
-// kPolyEvery; 0 = none). Measured on B200 at head dim 64: moving a quarter of
-// them lowered throughput (the exp unit is not the limit), so it is off.
-constexpr int kPolyEvery = 0;
+// Of the 16 exponential pairs in each 32-column chunk, kPolyPairs are computed
+// by a cubic on the f32x2 FMA pipe and the rest by MUFU ex2 (16 results per
+// clock per SM), so the two pipes share the softmax's exponentials.
+#ifndef LUNARA_ATTN_POLY_PAIRS
+#define LUNARA_ATTN_POLY_PAIRS 0
+#endif
+constexpr int kPolyPairs = LUNARA_ATTN_POLY_PAIRS;
+static_assert(kPolyPairs >= 0 && kPolyPairs <= 16, "poly pairs per chunk");
+// Ping-pong: the two softmax warpgroups take turns on the exponential phase
+// (an mbarrier hand-over), so one runs it while the other's MMAs run.
+#ifndef LUNARA_ATTN_PINGPONG
+#define LUNARA_ATTN_PINGPONG 0
+#endif
+constexpr bool kPingPong = LUNARA_ATTN_PINGPONG != 0;
 constexpr uint32_t kTileBytes = 128 * 128;  // one [128 x 64] 16-bit tile
 constexpr int kAttnSmem = 2 * kTileBytes + 2 * kKvStages * kTileBytes + 2 * 2 * kTileBytes + 256 + 1024;
 constexpr uint32_t kAttnTmemCols = 512;
@@ -87,7 +97,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* s_full = v_empty + kKvStages;   // [2]
   uint64_t* p_ready = s_full + 2;           // [2]
   uint64_t* o_full = p_ready + 2;           // [2]
-  uint64_t* drain_bar = o_full + 2;
+  uint64_t* turn = o_full + 2;              // [2] exp-phase hand-over (ping-pong)
+  uint64_t* drain_bar = turn + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -121,6 +132,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&s_full[w], 1);
       mbar_init(&p_ready[w], kQTile);
       mbar_init(&o_full[w], 1);
+      mbar_init(&turn[w], 4);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -288,16 +300,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int i = 0; i < 32; ++i)
             if (c * 32 + i >= lim) sc[c][i] = __float_as_uint(-INFINITY);
       }
-      // Row maximum with eight independent partial maxima (short dependency chains).
+      // Row maximum: three-input max, eight independent partial maxima.
       float mxp[8];
 #pragma unroll
       for (int t = 0; t < 8; ++t) mxp[t] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sc[c][i]));
-      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+        for (int i = 0; i < 32; i += 2)
+          mxp[(i >> 1) & 7] = fmax3(mxp[(i >> 1) & 7], __uint_as_float(sc[c][i]), __uint_as_float(sc[c][i + 1]));
+      const float mx = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7]));
       const float m_cand = mx * sl2;
       // P of the previous block must have been consumed (and O updated) before
       // P is overwritten and O is touched.
@@ -327,22 +339,41 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tmem_st_wait();
       }
       const float m_off = (m_used == -INFINITY) ? 0.f : m_used;
-      // P = exp2(S * scale * log2e - m), row sum, P -> swizzled K-major smem tile.
-      float sump[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if constexpr (kPingPong) {
+        // Warpgroup 0 goes first in each iteration; a wait is skipped when the
+        // other warpgroup has no iteration to hand over (causal or tail tiles).
+        const bool wait_turn = (w == 0) ? (j > 0 && j - 1 < nb1) : (j < nb0);
+        if (wait_turn) {
+          const uint32_t par = static_cast<uint32_t>(w == 0 ? j - 1 : j) & 1u;
+          if (!mbar_wait(&turn[w], par, abort_flag, err, kErrAttnSoftmax)) {
+            ok = false;
+            break;
+          }
+        }
+      }
+      // P = exp2(S * scale * log2e - m), row sum, P -> swizzled K-major smem tile,
+      // two columns per f32x2 instruction.
+      const uint64_t sl2x2 = f2_pack(sl2, sl2);
+      const uint64_t negm2 = f2_pack(-m_off, -m_off);
+      uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};   // packed (+0.0f, +0.0f)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          // One pair in kPolyEvery is computed on the FMA pipe, the rest on MUFU,
-          // so that both pipes share the exponentials.
-          const bool poly = kPolyEvery > 0 && ((c * 16 + i / 2) % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1;
-          const float x0 = fmaf(__uint_as_float(sc[c][i]), sl2, -m_off);
-          const float x1 = fmaf(__uint_as_float(sc[c][i + 1]), sl2, -m_off);
-          const float e0 = poly ? ex2_poly(x0) : ex2_approx(x0);
-          const float e1 = poly ? ex2_poly(x1) : ex2_approx(x1);
-          sump[(i >> 1) & 7] += e0 + e1;
-          pk[i / 2] = Io<T>::pack2(e0, e1);
+          const int pair = i >> 1;
+          const bool poly = ((pair * kPolyPairs) % 16) < kPolyPairs;   // spread evenly over the chunk
+          const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sc[c][i]), __uint_as_float(sc[c][i + 1])), sl2x2, negm2);
+          uint64_t e2;
+          if (poly) {
+            e2 = ex2_poly2(x2);
+          } else {
+            const float2 x = f2_unpack(x2);
+            e2 = f2_pack(ex2_approx(x.x), ex2_approx(x.y));
+          }
+          sum2[pair & 3] = f2_add(sum2[pair & 3], e2);
+          const float2 e = f2_unpack(e2);
+          pk[pair] = Io<T>::pack2(e.x, e.y);
         }
         uint8_t* chunk = myP + (c / 2) * kTileBytes + r * 128;
 #pragma unroll
@@ -352,7 +383,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
       }
-      l += ((sump[0] + sump[1]) + (sump[2] + sump[3])) + ((sump[4] + sump[5]) + (sump[6] + sump[7]));
+      const float2 ls = f2_unpack(f2_add(f2_add(sum2[0], sum2[1]), f2_add(sum2[2], sum2[3])));
+      l += ls.x + ls.y;
+      if constexpr (kPingPong) {
+        const bool give_turn = (w == 0) ? (j < nb1) : (j + 1 < nb0);
+        if (give_turn) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&turn[1 - w]);
+        }
+      }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_ready[w]);

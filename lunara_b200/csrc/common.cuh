@@ -378,6 +378,60 @@ __device__ __forceinline__ float ex2_poly(float x) {
   return __int_as_float(__float_as_int(p) + (j << 23));
 }
 
+// Pairs of fp32 values in one 64-bit register pair, for the sm_100 f32x2
+// instructions (one issue slot for two lanes of arithmetic).
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+__device__ __forceinline__ float2 f2_unpack(uint64_t r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// max(a, b, c) in one instruction (sm_100 three-input max).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// ex2_poly for a pair, with the additions and the cubic on the f32x2 pipe.
+__device__ __forceinline__ uint64_t ex2_poly2(uint64_t x2) {
+  float2 x = f2_unpack(x2);
+  const uint64_t xc = f2_pack(fmaxf(x.x, -126.0f), fmaxf(x.y, -126.0f));
+  const uint64_t t = f2_add(xc, f2_pack(12582912.0f, 12582912.0f));
+  const uint64_t f = f2_fma(f2_add(t, f2_pack(-12582912.0f, -12582912.0f)), f2_pack(-1.0f, -1.0f), xc);
+  uint64_t p = f2_fma(f2_pack(0.0551716685f, 0.0551716685f), f, f2_pack(0.2426111400f, 0.2426111400f));
+  p = f2_fma(p, f, f2_pack(0.6932609677f, 0.6932609677f));
+  p = f2_fma(p, f, f2_pack(0.9999280572f, 0.9999280572f));
+  const float2 tv = f2_unpack(t), pv = f2_unpack(p);
+  // (bits(t) - bits(1.5 * 2^23)) << 23 == bits(t) << 23 modulo 2^32.
+  return f2_pack(__uint_as_float(__float_as_uint(pv.x) + (__float_as_uint(tv.x) << 23)),
+                 __uint_as_float(__float_as_uint(pv.y) + (__float_as_uint(tv.y) << 23)));
+}
+
 __device__ __forceinline__ float tanh_approx(float x) {
   float y;
   asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));

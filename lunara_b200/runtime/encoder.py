@@ -20,6 +20,7 @@ Linear weights are kept as [out, in] (K-major for the tcgen05 B operand).
 from __future__ import annotations
 
 import math
+from collections import OrderedDict
 from typing import Callable, Dict, List, Optional
 
 import torch
@@ -84,6 +85,30 @@ class EncoderBlock:
     def _tile(self, name: str) -> Dict[str, int]:
         return self.gemm_tiles.get(name, {})
 
+    def kernel_fns(self, x: Optional[torch.Tensor] = None,
+                   out: Optional[torch.Tensor] = None) -> "OrderedDict[str, Callable[[], object]]":
+        """The seven launches of one block forward (x, default self.x -> out, default self.y),
+        in order, keyed by the names of KERNEL_ORDER."""
+        x = self.x if x is None else x
+        y = self.y if out is None else out
+        w = self.w
+        B, S, H, D = self.batch, self.seq, self.heads, self.head_dim
+        q, k, v = self._qkv_views()
+        o = self.attn.view(B, S, H, D).permute(0, 2, 1, 3)
+        return OrderedDict([
+            ("qkv_proj", lambda: ops.gemm(x, w["w_qkv"], self.qkv, bias=w["b_qkv"], b_layout="nk",
+                                          **self._tile("qkv_proj"))),
+            ("flash_attn", lambda: ops.attention(q, k, v, causal=False, scale=self.scale, out=o)),
+            ("out_proj", lambda: ops.gemm(self.attn, w["w_o"], self.h, bias=w["b_o"], residual=x, b_layout="nk",
+                                          **self._tile("out_proj"))),
+            ("layernorm_attn", lambda: ops.layernorm(self.h, w["ln1_w"], w["ln1_b"], self.eps, out=self.x1)),
+            ("ffn1", lambda: ops.gemm(self.x1, w["w_1"], self.f, bias=w["b_1"], activation=self.ffn_activation,
+                                      b_layout="nk", **self._tile("ffn1"))),
+            ("ffn2", lambda: ops.gemm(self.f, w["w_2"], self.g, bias=w["b_2"], residual=self.x1, b_layout="nk",
+                                      **self._tile("ffn2"))),
+            ("layernorm_ffn", lambda: ops.layernorm(self.g, w["ln2_w"], w["ln2_b"], self.eps, out=y)),
+        ])
+
     def run_kernels(self, x: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
                     hook: Optional[Callable[[str, str], None]] = None) -> torch.Tensor:
         """Launch the seven kernels on the current stream: x (default self.x) -> out (default self.y).
@@ -91,31 +116,13 @@ class EncoderBlock:
         ``hook(kernel_name, "begin"|"end")`` is called around each launch (used
         to record CUDA events inside a captured graph).
         """
-        x = self.x if x is None else x
         y = self.y if out is None else out
-        w = self.w
-        B, S, H, D = self.batch, self.seq, self.heads, self.head_dim
-
-        def step(name, fn):
+        for name, fn in self.kernel_fns(x, y).items():
             if hook:
                 hook(name, "begin")
             fn()
             if hook:
                 hook(name, "end")
-
-        step("qkv_proj", lambda: ops.gemm(x, w["w_qkv"], self.qkv, bias=w["b_qkv"], b_layout="nk",
-                                          **self._tile("qkv_proj")))
-        q, k, v = self._qkv_views()
-        o = self.attn.view(B, S, H, D).permute(0, 2, 1, 3)
-        step("flash_attn", lambda: ops.attention(q, k, v, causal=False, scale=self.scale, out=o))
-        step("out_proj", lambda: ops.gemm(self.attn, w["w_o"], self.h, bias=w["b_o"], residual=x, b_layout="nk",
-                                          **self._tile("out_proj")))
-        step("layernorm_attn", lambda: ops.layernorm(self.h, w["ln1_w"], w["ln1_b"], self.eps, out=self.x1))
-        step("ffn1", lambda: ops.gemm(self.x1, w["w_1"], self.f, bias=w["b_1"], activation=self.ffn_activation,
-                                      b_layout="nk", **self._tile("ffn1")))
-        step("ffn2", lambda: ops.gemm(self.f, w["w_2"], self.g, bias=w["b_2"], residual=self.x1, b_layout="nk",
-                                      **self._tile("ffn2")))
-        step("layernorm_ffn", lambda: ops.layernorm(self.g, w["ln2_w"], w["ln2_b"], self.eps, out=y))
         return y
 
 
