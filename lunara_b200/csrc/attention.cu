@@ -2,19 +2,19 @@
 //
 // tcgen05 path (f16 / bf16, D == 64): FlashAttention-style single pass with an
 // online softmax. One CTA owns 256 query rows of one (batch, head) as two
-// 128-row Q tiles, each with its own softmax warpgroup so that the tensor core
-// works on one tile while the other tile's softmax runs (ping-pong):
+// 128-row Q tiles, each with its own softmax warpgroup, sharing the K/V ring:
 //   warps 0-3   softmax warpgroup 0 (thread = query row of Q tile 0)
 //   warps 4-7   softmax warpgroup 1 (Q tile 1)
 //   warp 8      TMA producer: Q tiles once, K and V [128 x 64] blocks into a
 //               3-deep ring (128-byte swizzle, 4-D tensor maps over the
 //               caller's strides, so a fused QKV buffer is read in place)
 //   warp 9      TMEM allocator + single-thread tcgen05.mma issuer
-//                 S_w = Q_w K_j^T   (M=128, N=128, K=64)   -> TMEM
-//                 O_w = P_w V_j     (M=128, N=64,  K=128)  -> TMEM
-// The softmax warps read S from TMEM twice (row max, then exp2 + row sum),
-// write P as fp16/bf16 into a swizzled K-major shared tile for the PV MMA, and
-// fold each P V block into a register accumulator with the running rescale.
+//                 S_w = Q_w K_j^T   (M=128, N=128, K=64; A, B from shared memory)
+//                 O_w += P_w V_j    (M=128, N=64, K=128; A = P_w from TMEM)
+// Everything the softmax exchanges with the tensor core stays in TMEM: it
+// loads the whole S row once, hands the S buffer back at once (so S_w(j+1)
+// is computed while it works on block j), writes P as 16-bit pairs into TMEM
+// for the PV MMA, and O accumulates in TMEM with a lazily applied rescale.
 // Causal masking skips key blocks above the diagonal and masks the diagonal
 // block; heavy query blocks are scheduled first.
 // SIMT path: any D <= 256, any dtype, one warp per query row.
@@ -55,14 +55,13 @@ constexpr float kRescaleLog2 = 8.0f;
 #endif
 constexpr int kPolyPairs = LUNARA_ATTN_POLY_PAIRS;
 static_assert(kPolyPairs >= 0 && kPolyPairs <= 16, "poly pairs per chunk");
-// Ping-pong: the two softmax warpgroups take turns on the exponential phase
-// (an mbarrier hand-over), so one runs it while the other's MMAs run.
-#ifndef LUNARA_ATTN_PINGPONG
-#define LUNARA_ATTN_PINGPONG 0
-#endif
-constexpr bool kPingPong = LUNARA_ATTN_PINGPONG != 0;
 constexpr uint32_t kTileBytes = 128 * 128;  // one [128 x 64] 16-bit tile
-constexpr int kAttnSmem = 2 * kTileBytes + 2 * kKvStages * kTileBytes + 2 * 2 * kTileBytes + 256 + 1024;
+constexpr int kAttnSmem = 2 * kTileBytes + 2 * kKvStages * kTileBytes + 256 + 1024;
+// TMEM columns: S_w (128 fp32 columns per Q tile), O_w (64), P_w (128 16-bit
+// values packed in 64 columns).
+constexpr uint32_t kTmemS = 0;
+constexpr uint32_t kTmemO = 256;
+constexpr uint32_t kTmemP = 384;
 constexpr uint32_t kAttnTmemCols = 512;
 
 struct AttnParams {
@@ -87,18 +86,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sQ = smem;                                   // 2 tiles
   uint8_t* sK = sQ + 2 * kTileBytes;                    // kKvStages tiles
   uint8_t* sV = sK + kKvStages * kTileBytes;            // kKvStages tiles
-  uint8_t* sP = sV + kKvStages * kTileBytes;            // 2 x (2 tiles)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 4 * kTileBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kKvStages * kTileBytes);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = k_full + kKvStages;
   uint64_t* v_full = k_empty + kKvStages;
   uint64_t* v_empty = v_full + kKvStages;
-  uint64_t* s_full = v_empty + kKvStages;   // [2]
-  uint64_t* p_ready = s_full + 2;           // [2]
-  uint64_t* o_full = p_ready + 2;           // [2]
-  uint64_t* turn = o_full + 2;              // [2] exp-phase hand-over (ping-pong)
-  uint64_t* drain_bar = turn + 2;
+  uint64_t* s_full = v_empty + kKvStages;   // [2] S_w computed
+  uint64_t* s_free = s_full + 2;            // [2] S_w read into registers (buffer reusable)
+  uint64_t* p_ready = s_free + 2;           // [2] P_w written to TMEM
+  uint64_t* o_full = p_ready + 2;           // [2] P_w V done (O_w updated, P_w consumed)
+  uint64_t* drain_bar = o_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -130,9 +128,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     for (int w = 0; w < 2; ++w) {
       mbar_init(&s_full[w], 1);
+      mbar_init(&s_free[w], kQTile);
       mbar_init(&p_ready[w], kQTile);
       mbar_init(&o_full[w], 1);
-      mbar_init(&turn[w], 4);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -186,26 +184,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     reg_dealloc<kProducerRegs>();
     if (lane == 0) {
       // ---------------------------------------------------------- MMA issuer --
+      // Order per key block j: S_w(j+1) as soon as the softmax has pulled S_w(j)
+      // into registers (so the next scores are ready when it finishes block j),
+      // then P_w(j) V_j once P_w(j) is in TMEM.
       bool ok = mbar_wait(q_full, 0, abort_flag, err, kErrAttnMma);
       if (ok && nb > 0) {
         tc_fence_after();
         const uint32_t q_base = smem_u32(sQ);
-        const uint32_t p_base = smem_u32(sP);
         auto issue_s = [&](int w, int st) {
           const uint32_t q_addr = q_base + w * kTileBytes;
           const uint32_t k_addr = smem_u32(sK + st * kTileBytes);
 #pragma unroll
           for (int k = 0; k < kHeadDim / 16; ++k)
-            umma_f16_ss(tmem_base + w * 128, sw128_desc(q_addr + k * 32, 16, 1024),
+            umma_f16_ss(tmem_base + kTmemS + w * 128, sw128_desc(q_addr + k * 32, 16, 1024),
                         sw128_desc(k_addr + k * 32, 16, 1024), IDESC_S, k > 0 ? 1u : 0u);
         };
         auto issue_pv = [&](int w, int st, int j) {
-          const uint32_t p_addr = p_base + w * 2 * kTileBytes;
           const uint32_t v_addr = smem_u32(sV + st * kTileBytes);
 #pragma unroll
           for (int k = 0; k < kKvBlock / 16; ++k)
-            umma_f16_ss(tmem_base + 256 + w * 128,
-                        sw128_desc(p_addr + (k / 4) * kTileBytes + (k % 4) * 32, 16, 1024),
+            umma_f16_ts(tmem_base + kTmemO + w * kHeadDim, tmem_base + kTmemP + w * (kKvBlock / 2) + k * 8,
                         sw128_desc(v_addr + k * 2048, kTileBytes, 1024), IDESC_PV, (j > 0 || k > 0) ? 1u : 0u);
         };
         ok = mbar_wait(&k_full[0], 0, abort_flag, err, kErrAttnMma);
@@ -222,29 +220,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int j = 0; j < nb && ok; ++j) {
           const int st = j % kKvStages;
           const uint32_t ph = static_cast<uint32_t>(j / kKvStages) & 1u;
-          const bool has_next = j + 1 < nb;
-          const int st1 = (j + 1) % kKvStages;
-          const uint32_t ph1 = static_cast<uint32_t>((j + 1) / kKvStages) & 1u;
-          if (!mbar_wait(&v_full[st], ph, abort_flag, err, kErrAttnMma)) { ok = false; break; }
-          if (has_next && !mbar_wait(&k_full[st1], ph1, abort_flag, err, kErrAttnMma)) { ok = false; break; }
-          for (int w = 0; w < 2 && ok; ++w) {
-            const int nbw = w ? nb1 : nb0;
-            if (j >= nbw) continue;
-            if (!mbar_wait(&p_ready[w], static_cast<uint32_t>(j) & 1u, abort_flag, err, kErrAttnMma)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_pv(w, st, j);
-            umma_commit(&o_full[w]);
-            if (j + 1 < nbw) {
+          const uint32_t jpar = static_cast<uint32_t>(j) & 1u;
+          if (j + 1 < nb) {
+            const int st1 = (j + 1) % kKvStages;
+            const uint32_t ph1 = static_cast<uint32_t>((j + 1) / kKvStages) & 1u;
+            if (!mbar_wait(&k_full[st1], ph1, abort_flag, err, kErrAttnMma)) { ok = false; break; }
+            for (int w = 0; w < 2 && ok; ++w) {
+              if (j + 1 >= (w ? nb1 : nb0)) continue;
+              if (!mbar_wait(&s_free[w], jpar, abort_flag, err, kErrAttnMma)) { ok = false; break; }
+              tc_fence_after();
               issue_s(w, st1);
               umma_commit(&s_full[w]);
             }
+            if (!ok) break;
+            umma_commit(&k_empty[st1]);
+          }
+          if (!mbar_wait(&v_full[st], ph, abort_flag, err, kErrAttnMma)) { ok = false; break; }
+          for (int w = 0; w < 2 && ok; ++w) {
+            if (j >= (w ? nb1 : nb0)) continue;
+            if (!mbar_wait(&p_ready[w], jpar, abort_flag, err, kErrAttnMma)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(w, st, j);
+            umma_commit(&o_full[w]);
           }
           if (!ok) break;
           umma_commit(&v_empty[st]);
-          if (has_next) umma_commit(&k_empty[st1]);
         }
       }
       if (!ok) {
@@ -268,9 +268,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int q_first = q0 + w * kQTile;
     const int my_nb = w ? nb1 : nb0;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tS = tmem_base + lane_off + w * 128;
-    const uint32_t tO = tmem_base + lane_off + 256 + w * 128;
-    uint8_t* myP = sP + w * 2 * kTileBytes;
+    const uint32_t tS = tmem_base + lane_off + kTmemS + w * 128;
+    const uint32_t tO = tmem_base + lane_off + kTmemO + w * kHeadDim;
+    const uint32_t tP = tmem_base + lane_off + kTmemP + w * (kKvBlock / 2);
     const float sl2 = p.scale_log2;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
@@ -281,7 +281,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         break;
       }
       tc_fence_after();
-      // The whole 128-column score row: four TMEM loads, one wait.
+      // The whole 128-column score row: four TMEM loads, one wait; then the S
+      // buffer is handed back so the next block's scores can be computed.
       uint32_t sc[4][32];
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tS + c * 32, sc[c]);
@@ -289,6 +290,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       reg_fence(sc[1]);
       reg_fence(sc[2]);
       reg_fence(sc[3]);
+      tc_fence_before();
+      mbar_arrive(&s_free[w]);
       const int kv0 = j * kKvBlock;
       if ((kv0 + kKvBlock > p.Skv) || (p.causal && kv0 + kKvBlock - 1 > q_first)) {
         // Keep key columns < Skv and (causal) <= this query row.
@@ -311,8 +314,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           mxp[(i >> 1) & 7] = fmax3(mxp[(i >> 1) & 7], __uint_as_float(sc[c][i]), __uint_as_float(sc[c][i + 1]));
       const float mx = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7]));
       const float m_cand = mx * sl2;
-      // P of the previous block must have been consumed (and O updated) before
-      // P is overwritten and O is touched.
+      // The previous block's P V must be complete (P_w consumed, O_w updated)
+      // before P_w is overwritten and O_w is touched.
       if (j > 0) {
         if (!mbar_wait(&o_full[w], static_cast<uint32_t>(j - 1) & 1u, abort_flag, err, kErrAttnSoftmax)) {
           ok = false;
@@ -327,32 +330,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const float alpha = ex2_approx(m_used - m_next);
         l *= alpha;
         m_used = m_next;
+        const uint64_t a2 = f2_pack(alpha, alpha);
 #pragma unroll
         for (int c = 0; c < kHeadDim / 32; ++c) {
           uint32_t ov[32];
           tmem_ld_32x32b_x32(tO + c * 32, ov);
           tmem_ld_wait_regs(ov);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+          for (int i = 0; i < 32; i += 2) {
+            const float2 v2 = f2_unpack(f2_mul(f2_pack(__uint_as_float(ov[i]), __uint_as_float(ov[i + 1])), a2));
+            ov[i] = __float_as_uint(v2.x);
+            ov[i + 1] = __float_as_uint(v2.y);
+          }
           tmem_st_32x32b_x32(tO + c * 32, ov);
         }
-        tmem_st_wait();
       }
       const float m_off = (m_used == -INFINITY) ? 0.f : m_used;
-      if constexpr (kPingPong) {
-        // Warpgroup 0 goes first in each iteration; a wait is skipped when the
-        // other warpgroup has no iteration to hand over (causal or tail tiles).
-        const bool wait_turn = (w == 0) ? (j > 0 && j - 1 < nb1) : (j < nb0);
-        if (wait_turn) {
-          const uint32_t par = static_cast<uint32_t>(w == 0 ? j - 1 : j) & 1u;
-          if (!mbar_wait(&turn[w], par, abort_flag, err, kErrAttnSoftmax)) {
-            ok = false;
-            break;
-          }
-        }
-      }
-      // P = exp2(S * scale * log2e - m), row sum, P -> swizzled K-major smem tile,
-      // two columns per f32x2 instruction.
+      // P = exp2(S * scale * log2e - m) as 16-bit pairs into TMEM (the A
+      // operand of the PV MMA), row sum in fp32; two columns per f32x2 op.
       const uint64_t sl2x2 = f2_pack(sl2, sl2);
       const uint64_t negm2 = f2_pack(-m_off, -m_off);
       uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};   // packed (+0.0f, +0.0f)
@@ -375,24 +370,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const float2 e = f2_unpack(e2);
           pk[pair] = Io<T>::pack2(e.x, e.y);
         }
-        uint8_t* chunk = myP + (c / 2) * kTileBytes + r * 128;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int u = (c % 2) * 4 + q;
-          *reinterpret_cast<uint4*>(chunk + ((u ^ (r & 7)) * 16)) =
-              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-        }
+        tmem_st_32x32b_x16(tP + c * 16, pk);
       }
       const float2 ls = f2_unpack(f2_add(f2_add(sum2[0], sum2[1]), f2_add(sum2[2], sum2[3])));
       l += ls.x + ls.y;
-      if constexpr (kPingPong) {
-        const bool give_turn = (w == 0) ? (j < nb1) : (j + 1 < nb0);
-        if (give_turn) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&turn[1 - w]);
-        }
-      }
-      fence_proxy_async_smem();
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_ready[w]);
     }
