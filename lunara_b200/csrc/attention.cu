@@ -8,7 +8,7 @@
 //   warp 8      TMA producer: Q tiles once, K and V [128 x 64] blocks into a
 //               3-deep ring (128-byte swizzle, 4-D tensor maps over the
 //               caller's strides, so a fused QKV buffer is read in place)
-//   warp 9      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 9-10  tcgen05.mma issuers, one per Q tile (warp 9 also allocates TMEM)
 //                 S_w = Q_w K_j^T   (M=128, N=128, K=64; A, B from shared memory)
 //                 O_w += P_w V_j    (M=128, N=64, K=128; A = P_w from TMEM)
 // Everything the softmax exchanges with the tensor core stays in TMEM: it
@@ -38,7 +38,7 @@ constexpr int kQTile = 128;     // query rows per softmax warpgroup
 constexpr int kKvBlock = 128;   // keys per iteration
 constexpr int kHeadDim = 64;
 constexpr int kKvStages = 3;
-constexpr int kAttnThreads = 384;  // warpgroups: 0-1 softmax, 2 = TMA warp, MMA warp, 2 idle warps
+constexpr int kAttnThreads = 384;  // warpgroups: 0-1 softmax, 2 = TMA warp, 2 MMA warps, 1 idle warp
 // Register split with setmaxnreg: the kernel launches with 168 registers per
 // thread (384 x 168 = 64512); warpgroup 2 drops to 56 and the two softmax
 // warpgroups rise to 224: 128 x 56 + 256 x 224 = 64512, exactly the launch total.
@@ -96,8 +96,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* s_free = s_full + 2;            // [2] S_w read into registers (buffer reusable)
   uint64_t* p_ready = s_free + 2;           // [2] P_w written to TMEM
   uint64_t* o_full = p_ready + 2;           // [2] P_w V done (O_w updated, P_w consumed)
-  uint64_t* drain_bar = o_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* drain_bar = o_full + 2;         // [2] one per MMA issuer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -122,9 +122,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     mbar_init(q_full, 1);
     for (int s = 0; s < kKvStages; ++s) {
       mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
+      mbar_init(&k_empty[s], 2);
       mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
+      mbar_init(&v_empty[s], 2);
     }
     for (int w = 0; w < 2; ++w) {
       mbar_init(&s_full[w], 1);
@@ -132,7 +132,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&p_ready[w], kQTile);
       mbar_init(&o_full[w], 1);
     }
-    mbar_init(drain_bar, 1);
+    mbar_init(&drain_bar[0], 1);
+    mbar_init(&drain_bar[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -180,80 +181,98 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           mbar_drain_wait(&v_full[i % kKvStages], static_cast<uint32_t>(i / kKvStages) & 1u, 1000000000ull);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == 9 || warp == 10) {
     reg_dealloc<kProducerRegs>();
     if (lane == 0) {
-      // ---------------------------------------------------------- MMA issuer --
-      // Order per key block j: S_w(j+1) as soon as the softmax has pulled S_w(j)
-      // into registers (so the next scores are ready when it finishes block j),
-      // then P_w(j) V_j once P_w(j) is in TMEM.
+      // ------------------------------------------------------ MMA issuers --
+      // Warp 9 issues the MMAs of Q tile 0, warp 10 those of Q tile 1, so that
+      // neither tile's MMAs queue behind the other's events. Per key block j:
+      // S_w(j+1) as soon as the softmax has pulled S_w(j) into registers (the
+      // next scores are ready when it finishes block j), then P_w(j) V_j once
+      // P_w(j) is in TMEM. Both issuers release every K/V stage (the empty
+      // barriers count two arrivals); blocks past this tile's last one are
+      // released once loaded, so each arrival lands on the phase of its block.
+      const int w = warp - 9;
+      const int nbw = w ? nb1 : nb0;
       bool ok = mbar_wait(q_full, 0, abort_flag, err, kErrAttnMma);
       if (ok && nb > 0) {
         tc_fence_after();
-        const uint32_t q_base = smem_u32(sQ);
-        auto issue_s = [&](int w, int st) {
-          const uint32_t q_addr = q_base + w * kTileBytes;
-          const uint32_t k_addr = smem_u32(sK + st * kTileBytes);
+        // Descriptors are built once; the start-address field (bits 0-13, in
+        // 16-byte units) then moves by constants: +32 B per K step within a
+        // K-major row (Q, K), +2048 B (16 rows of 128 B) per K step down V,
+        // and one tile (16 KB) per ring stage.
+        constexpr uint64_t kTileStep = kTileBytes >> 4;
+        const uint64_t qd = sw128_desc(smem_u32(sQ + w * kTileBytes), 16, 1024);
+        const uint64_t kd0 = sw128_desc(smem_u32(sK), 16, 1024);
+        const uint64_t vd0 = sw128_desc(smem_u32(sV), kTileBytes, 1024);
+        const uint32_t d_s = tmem_base + kTmemS + w * 128;
+        const uint32_t d_o = tmem_base + kTmemO + w * kHeadDim;
+        const uint32_t a_p = tmem_base + kTmemP + w * (kKvBlock / 2);
+        auto issue_s = [&](int st) {
+          const uint64_t kd = kd0 + st * kTileStep;
 #pragma unroll
           for (int k = 0; k < kHeadDim / 16; ++k)
-            umma_f16_ss(tmem_base + kTmemS + w * 128, sw128_desc(q_addr + k * 32, 16, 1024),
-                        sw128_desc(k_addr + k * 32, 16, 1024), IDESC_S, k > 0 ? 1u : 0u);
+            umma_f16_ss(d_s, qd + 2 * k, kd + 2 * k, IDESC_S, k > 0 ? 1u : 0u);
         };
-        auto issue_pv = [&](int w, int st, int j) {
-          const uint32_t v_addr = smem_u32(sV + st * kTileBytes);
+        auto issue_pv = [&](int st, int j) {
+          const uint64_t vd = vd0 + st * kTileStep;
 #pragma unroll
           for (int k = 0; k < kKvBlock / 16; ++k)
-            umma_f16_ts(tmem_base + kTmemO + w * kHeadDim, tmem_base + kTmemP + w * (kKvBlock / 2) + k * 8,
-                        sw128_desc(v_addr + k * 2048, kTileBytes, 1024), IDESC_PV, (j > 0 || k > 0) ? 1u : 0u);
+            umma_f16_ts(d_o, a_p + k * 8, vd + 128 * k, IDESC_PV, (j > 0 || k > 0) ? 1u : 0u);
         };
         ok = mbar_wait(&k_full[0], 0, abort_flag, err, kErrAttnMma);
         if (ok) {
           tc_fence_after();
-          for (int w = 0; w < 2; ++w) {
-            if ((w ? nb1 : nb0) > 0) {
-              issue_s(w, 0);
-              umma_commit(&s_full[w]);
-            }
+          if (nbw > 0) {
+            issue_s(0);
+            umma_commit(&s_full[w]);
+            umma_commit(&k_empty[0]);
+          } else {
+            mbar_arrive(&k_empty[0]);
           }
-          umma_commit(&k_empty[0]);
         }
         for (int j = 0; j < nb && ok; ++j) {
           const int st = j % kKvStages;
           const uint32_t ph = static_cast<uint32_t>(j / kKvStages) & 1u;
-          const uint32_t jpar = static_cast<uint32_t>(j) & 1u;
           if (j + 1 < nb) {
             const int st1 = (j + 1) % kKvStages;
             const uint32_t ph1 = static_cast<uint32_t>((j + 1) / kKvStages) & 1u;
             if (!mbar_wait(&k_full[st1], ph1, abort_flag, err, kErrAttnMma)) { ok = false; break; }
-            for (int w = 0; w < 2 && ok; ++w) {
-              if (j + 1 >= (w ? nb1 : nb0)) continue;
-              if (!mbar_wait(&s_free[w], jpar, abort_flag, err, kErrAttnMma)) { ok = false; break; }
+            if (j + 1 < nbw) {
+              if (!mbar_wait(&s_free[w], static_cast<uint32_t>(j) & 1u, abort_flag, err, kErrAttnMma)) {
+                ok = false;
+                break;
+              }
               tc_fence_after();
-              issue_s(w, st1);
+              issue_s(st1);
               umma_commit(&s_full[w]);
+              umma_commit(&k_empty[st1]);
+            } else {
+              mbar_arrive(&k_empty[st1]);
             }
-            if (!ok) break;
-            umma_commit(&k_empty[st1]);
           }
           if (!mbar_wait(&v_full[st], ph, abort_flag, err, kErrAttnMma)) { ok = false; break; }
-          for (int w = 0; w < 2 && ok; ++w) {
-            if (j >= (w ? nb1 : nb0)) continue;
-            if (!mbar_wait(&p_ready[w], jpar, abort_flag, err, kErrAttnMma)) { ok = false; break; }
+          if (j < nbw) {
+            if (!mbar_wait(&p_ready[w], static_cast<uint32_t>(j) & 1u, abort_flag, err, kErrAttnMma)) {
+              ok = false;
+              break;
+            }
             tc_fence_after();
-            issue_pv(w, st, j);
+            issue_pv(st, j);
             umma_commit(&o_full[w]);
+            umma_commit(&v_empty[st]);
+          } else {
+            mbar_arrive(&v_empty[st]);
           }
-          if (!ok) break;
-          umma_commit(&v_empty[st]);
         }
       }
       if (!ok) {
-        umma_commit(drain_bar);
-        mbar_drain_wait(drain_bar, 0, 1000000000ull);
+        umma_commit(drain_bar + w);
+        mbar_drain_wait(drain_bar + w, 0, 1000000000ull);
       }
     }
-  } else if (warp >= 10) {
-    reg_dealloc<kProducerRegs>();   // idle warps of warpgroup 2
+  } else if (warp == 11) {
+    reg_dealloc<kProducerRegs>();   // idle warp of warpgroup 2
   } else {
     reg_alloc<kSoftmaxRegs>();
     // ------------------------------------------------------------- softmax --
@@ -314,8 +333,50 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           mxp[(i >> 1) & 7] = fmax3(mxp[(i >> 1) & 7], __uint_as_float(sc[c][i]), __uint_as_float(sc[c][i + 1]));
       const float mx = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7]));
       const float m_cand = mx * sl2;
+      // Running maximum: raised only when a row's maximum grows by more than
+      // 2^kRescaleLog2 (decided warp-wide); O is rescaled below, once the
+      // previous block's P V has landed.
+      bool rescale = false;
+      float alpha = 1.f;
+      if (j == 0) {
+        m_used = m_cand;
+      } else if (__any_sync(0xffffffffu, m_cand > m_used + kRescaleLog2)) {
+        const float m_next = fmaxf(m_used, m_cand);
+        alpha = ex2_approx(m_used - m_next);
+        l *= alpha;
+        m_used = m_next;
+        rescale = true;
+      }
+      const float m_off = (m_used == -INFINITY) ? 0.f : m_used;
+      // P = exp2(S * scale * log2e - m) as 16-bit pairs held in registers, row
+      // sum in fp32; two columns per f32x2 op.
+      const uint64_t sl2x2 = f2_pack(sl2, sl2);
+      const uint64_t negm2 = f2_pack(-m_off, -m_off);
+      uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};   // packed (+0.0f, +0.0f)
+      uint32_t pk[4][16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const int pair = i >> 1;
+          const bool poly = ((pair * kPolyPairs) % 16) < kPolyPairs;   // spread evenly over the chunk
+          const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sc[c][i]), __uint_as_float(sc[c][i + 1])), sl2x2, negm2);
+          uint64_t e2;
+          if (poly) {
+            e2 = ex2_poly2(x2);
+          } else {
+            const float2 x = f2_unpack(x2);
+            e2 = f2_pack(ex2_approx(x.x), ex2_approx(x.y));
+          }
+          sum2[pair & 3] = f2_add(sum2[pair & 3], e2);
+          const float2 e = f2_unpack(e2);
+          pk[c][pair] = Io<T>::pack2(e.x, e.y);
+        }
+      }
+      const float2 ls = f2_unpack(f2_add(f2_add(sum2[0], sum2[1]), f2_add(sum2[2], sum2[3])));
+      l += ls.x + ls.y;
       // The previous block's P V must be complete (P_w consumed, O_w updated)
-      // before P_w is overwritten and O_w is touched.
+      // before P_w is overwritten and O_w is rescaled; by now it normally is.
       if (j > 0) {
         if (!mbar_wait(&o_full[w], static_cast<uint32_t>(j - 1) & 1u, abort_flag, err, kErrAttnSoftmax)) {
           ok = false;
@@ -323,13 +384,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         tc_fence_after();
       }
-      if (j == 0) {
-        m_used = m_cand;
-      } else if (__any_sync(0xffffffffu, m_cand > m_used + kRescaleLog2)) {
-        const float m_next = fmaxf(m_used, m_cand);
-        const float alpha = ex2_approx(m_used - m_next);
-        l *= alpha;
-        m_used = m_next;
+      if (rescale) {
         const uint64_t a2 = f2_pack(alpha, alpha);
 #pragma unroll
         for (int c = 0; c < kHeadDim / 32; ++c) {
@@ -345,35 +400,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tmem_st_32x32b_x32(tO + c * 32, ov);
         }
       }
-      const float m_off = (m_used == -INFINITY) ? 0.f : m_used;
-      // P = exp2(S * scale * log2e - m) as 16-bit pairs into TMEM (the A
-      // operand of the PV MMA), row sum in fp32; two columns per f32x2 op.
-      const uint64_t sl2x2 = f2_pack(sl2, sl2);
-      const uint64_t negm2 = f2_pack(-m_off, -m_off);
-      uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};   // packed (+0.0f, +0.0f)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const int pair = i >> 1;
-          const bool poly = ((pair * kPolyPairs) % 16) < kPolyPairs;   // spread evenly over the chunk
-          const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sc[c][i]), __uint_as_float(sc[c][i + 1])), sl2x2, negm2);
-          uint64_t e2;
-          if (poly) {
-            e2 = ex2_poly2(x2);
-          } else {
-            const float2 x = f2_unpack(x2);
-            e2 = f2_pack(ex2_approx(x.x), ex2_approx(x.y));
-          }
-          sum2[pair & 3] = f2_add(sum2[pair & 3], e2);
-          const float2 e = f2_unpack(e2);
-          pk[pair] = Io<T>::pack2(e.x, e.y);
-        }
-        tmem_st_32x32b_x16(tP + c * 16, pk);
-      }
-      const float2 ls = f2_unpack(f2_add(f2_add(sum2[0], sum2[1]), f2_add(sum2[2], sum2[3])));
-      l += ls.x + ls.y;
+      for (int c = 0; c < 4; ++c) tmem_st_32x32b_x16(tP + c * 16, pk[c]);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_ready[w]);
