@@ -353,14 +353,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (warp == 0 && lane == 0 && static_cast<int>(blockIdx.x) < num_tiles) {
+    // Before the predecessor has finished: descriptors, and the first ring's
+    // worth of B (typically weights, cold after other work) into L2.
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+    const int n0 = (static_cast<int>(blockIdx.x) / m_tiles) * BN;
+    for (int kb = 0; kb < kblocks && kb < STAGES; ++kb) {
+      if constexpr (B_KMAJOR) {
+        tma_prefetch_l2_2d(&tma_b, kb * BK, n0);
+      } else {
+#pragma unroll
+        for (int j = 0; j < BN / 64; ++j) tma_prefetch_l2_2d(&tma_b, n0 + j * 64, kb * BK);
+      }
+    }
+  }
   pdl_wait();
   pdl_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------ TMA producer --
-      tma_prefetch_desc(&tma_a);
-      tma_prefetch_desc(&tma_b);
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
@@ -562,14 +575,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   cluster_sync();   // barriers of both CTAs initialised before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (warp == 0 && lane == 0 && cluster_id < num_tiles) {
+    // Before the predecessor has finished: descriptors, and this CTA's half of
+    // the first ring's worth of B into L2.
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+    const int nb0 = (cluster_id / m_tiles) * BN + static_cast<int>(rank) * BH;
+    for (int kb = 0; kb < kblocks && kb < STAGES; ++kb) {
+      if constexpr (B_KMAJOR) {
+        tma_prefetch_l2_2d(&tma_b, kb * BK, nb0);
+      } else {
+#pragma unroll
+        for (int j = 0; j < BH / 64; ++j) tma_prefetch_l2_2d(&tma_b, nb0 + j * 64, kb * BK);
+      }
+    }
+  }
   pdl_wait();
   pdl_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------ TMA producer --
-      tma_prefetch_desc(&tma_a);
-      tma_prefetch_desc(&tma_b);
       uint32_t stage = 0, phase = 0;
       bool ok = true;
       for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
