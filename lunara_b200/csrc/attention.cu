@@ -1,22 +1,25 @@
 // Scaled-dot-product attention forward, O = softmax(Q K^T * scale [+ causal]) V.
 //
 // tcgen05 path (f16 / bf16, D == 64): FlashAttention-style single pass with an
-// online softmax. One CTA owns 256 query rows of one (batch, head) as two
-// 128-row Q tiles, each with its own softmax warpgroup, sharing the K/V ring:
-//   warps 0-3   softmax warpgroup 0 (thread = query row of Q tile 0)
-//   warps 4-7   softmax warpgroup 1 (Q tile 1)
-//   warp 8      TMA producer: Q tiles once, K and V [128 x 64] blocks into a
-//               3-deep ring (128-byte swizzle, 4-D tensor maps over the
+// online softmax. One CTA owns one 128-row Q tile of one (batch, head); its two
+// halves split the key blocks (half 0 takes blocks 0, 2, 4, ..., half 1 takes
+// 1, 3, 5, ...), each keeping its own running max, row sum and O, and merge
+// them at the end. One tile per CTA gives twice as many CTAs as tile pairs
+// would, which evens out the last wave on 148 SMs.
+//   warps 0-3   softmax warpgroup 0 (thread = query row), half 0
+//   warps 4-7   softmax warpgroup 1 (same rows), half 1
+//   warp 8      TMA producer: the Q tile once, K and V [128 x 64] blocks into a
+//               4-deep ring (128-byte swizzle, 4-D tensor maps over the
 //               caller's strides, so a fused QKV buffer is read in place)
-//   warps 9-10  tcgen05.mma issuers, one per Q tile (warp 9 also allocates TMEM)
-//                 S_w = Q_w K_j^T   (M=128, N=128, K=64; A, B from shared memory)
+//   warps 9-10  tcgen05.mma issuers, one per half (warp 9 also allocates TMEM)
+//                 S_w = Q K_j^T     (M=128, N=128, K=64; A, B from shared memory)
 //                 O_w += P_w V_j    (M=128, N=64, K=128; A = P_w from TMEM)
 // Everything the softmax exchanges with the tensor core stays in TMEM: it
-// loads the whole S row once, hands the S buffer back at once (so S_w(j+1)
-// is computed while it works on block j), writes P as 16-bit pairs into TMEM
-// for the PV MMA, and O accumulates in TMEM with a lazily applied rescale.
-// Causal masking skips key blocks above the diagonal and masks the diagonal
-// block; heavy query blocks are scheduled first.
+// loads the whole S row once, hands the S buffer back at once (so the half's
+// next scores are computed while it works on the current block), writes P as
+// 16-bit pairs into TMEM for the PV MMA, and O accumulates in TMEM with a
+// lazily applied rescale. Causal masking skips key blocks above the diagonal
+// and masks the diagonal block; the heaviest tiles are scheduled first.
 // SIMT path: any D <= 256, any dtype, one warp per query row.
 //
 // Semantics follow lunara/codegen/triton_emitter.py:212-293: scale applied to
@@ -37,7 +40,7 @@ namespace {
 constexpr int kQTile = 128;     // query rows per softmax warpgroup
 constexpr int kKvBlock = 128;   // keys per iteration
 constexpr int kHeadDim = 64;
-constexpr int kKvStages = 3;
+constexpr int kKvStages = 4;
 constexpr int kAttnThreads = 384;  // warpgroups: 0-1 softmax, 2 = TMA warp, 2 MMA warps, 1 idle warp
 // Register split with setmaxnreg: the kernel launches with 168 registers per
 // thread (384 x 168 = 64512); warpgroup 2 drops to 56 and the two softmax
@@ -56,7 +59,7 @@ constexpr float kRescaleLog2 = 8.0f;
 constexpr int kPolyPairs = LUNARA_ATTN_POLY_PAIRS;
 static_assert(kPolyPairs >= 0 && kPolyPairs <= 16, "poly pairs per chunk");
 constexpr uint32_t kTileBytes = 128 * 128;  // one [128 x 64] 16-bit tile
-constexpr int kAttnSmem = 2 * kTileBytes + 2 * kKvStages * kTileBytes + 256 + 1024;
+constexpr int kAttnSmem = kTileBytes + 2 * kKvStages * kTileBytes + 4 * kQTile * 4 + 256 + 1024;
 // TMEM columns: S_w (128 fp32 columns per Q tile), O_w (64), P_w (128 16-bit
 // values packed in 64 columns).
 constexpr uint32_t kTmemS = 0;
@@ -68,7 +71,7 @@ struct AttnParams {
   void* O;
   int64_t os_b, os_h, os_s;
   int H, Sq, Skv;
-  int n_qblocks;
+  int n_qtiles;
   float scale_log2;
   int causal;
 };
@@ -83,10 +86,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
-  uint8_t* sQ = smem;                                   // 2 tiles
-  uint8_t* sK = sQ + 2 * kTileBytes;                    // kKvStages tiles
+  uint8_t* sQ = smem;                                   // the Q tile
+  uint8_t* sK = sQ + kTileBytes;                        // kKvStages tiles
   uint8_t* sV = sK + kKvStages * kTileBytes;            // kKvStages tiles
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kKvStages * kTileBytes);
+  float* s_stats = reinterpret_cast<float*>(sV + kKvStages * kTileBytes);   // [half][m | l][row]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_stats + 2 * 2 * kQTile);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = k_full + kKvStages;
@@ -96,44 +100,43 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* s_free = s_full + 2;            // [2] S_w read into registers (buffer reusable)
   uint64_t* p_ready = s_free + 2;           // [2] P_w written to TMEM
   uint64_t* o_full = p_ready + 2;           // [2] P_w V done (O_w updated, P_w consumed)
-  uint64_t* drain_bar = o_full + 2;         // [2] one per MMA issuer
+  uint64_t* stats_ready = o_full + 2;       // both halves' O, m, l final
+  uint64_t* drain_bar = stats_ready + 1;    // [2] one per MMA issuer
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int qb = p.causal ? (p.n_qblocks - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
+  const int qt = p.causal ? (p.n_qtiles - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
   const int h = blockIdx.y;
   const int b = blockIdx.z;
-  const int q0 = qb * 2 * kQTile;
+  const int q0 = qt * kQTile;
+  // Key blocks of this Q tile: 0 .. nb-1 (causal: up to the diagonal block).
+  // Half w of the CTA (softmax warpgroup w and MMA warp 9+w) takes blocks j = w, w+2, ...
   const int nb_total = (p.Skv + kKvBlock - 1) / kKvBlock;
-  // Key blocks each Q tile visits (0 for a tile past the end of the sequence).
-  auto blocks_for = [&](int first) {
-    if (first >= p.Sq) return 0;
-    if (!p.causal) return nb_total;
-    const int lim = (first + kQTile - 1) / kKvBlock + 1;
-    return lim < nb_total ? lim : nb_total;
-  };
-  const int nb0 = blocks_for(q0);
-  const int nb1 = blocks_for(q0 + kQTile);
-  const int nb = nb0 > nb1 ? nb0 : nb1;
+  int nb = nb_total;
+  if (p.causal) {
+    const int lim = (q0 + kQTile - 1) / kKvBlock + 1;
+    nb = lim < nb_total ? lim : nb_total;
+  }
+  const int nb_h0 = (nb + 1) / 2, nb_h1 = nb / 2;   // blocks of half 0 / half 1
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < kKvStages; ++s) {
       mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 2);
+      mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 2);
+      mbar_init(&v_empty[s], 1);
     }
     for (int w = 0; w < 2; ++w) {
       mbar_init(&s_full[w], 1);
       mbar_init(&s_free[w], kQTile);
       mbar_init(&p_ready[w], kQTile);
       mbar_init(&o_full[w], 1);
+      mbar_init(&drain_bar[w], 1);
     }
-    mbar_init(&drain_bar[0], 1);
-    mbar_init(&drain_bar[1], 1);
+    mbar_init(stats_ready, 2 * kQTile);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -156,9 +159,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tma_prefetch_desc(&tq);
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
-      mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
+      mbar_arrive_expect_tx(q_full, kTileBytes);
       tma_load_4d(sQ, &tq, q_full, 0, q0, h, b);
-      tma_load_4d(sQ + kTileBytes, &tq, q_full, 0, q0 + kQTile, h, b);
       int issued_k = 0, issued_v = 0;
       bool ok = true;
       for (int j = 0; j < nb && ok; ++j) {
@@ -185,24 +187,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     reg_dealloc<kProducerRegs>();
     if (lane == 0) {
       // ------------------------------------------------------ MMA issuers --
-      // Warp 9 issues the MMAs of Q tile 0, warp 10 those of Q tile 1, so that
-      // neither tile's MMAs queue behind the other's events. Per key block j:
-      // S_w(j+1) as soon as the softmax has pulled S_w(j) into registers (the
+      // Warp 9 + w issues the MMAs of half w, for its key blocks j = w + 2i:
+      // S_w(next) as soon as the softmax has pulled S_w(j) into registers (the
       // next scores are ready when it finishes block j), then P_w(j) V_j once
-      // P_w(j) is in TMEM. Both issuers release every K/V stage (the empty
-      // barriers count two arrivals); blocks past this tile's last one are
-      // released once loaded, so each arrival lands on the phase of its block.
+      // P_w(j) is in TMEM. Each ring stage holds one key block and is released
+      // by the issuer of the half that uses it.
       const int w = warp - 9;
-      const int nbw = w ? nb1 : nb0;
+      const int nbw = w ? nb_h1 : nb_h0;
       bool ok = mbar_wait(q_full, 0, abort_flag, err, kErrAttnMma);
-      if (ok && nb > 0) {
+      if (ok && nbw > 0) {
         tc_fence_after();
         // Descriptors are built once; the start-address field (bits 0-13, in
         // 16-byte units) then moves by constants: +32 B per K step within a
         // K-major row (Q, K), +2048 B (16 rows of 128 B) per K step down V,
         // and one tile (16 KB) per ring stage.
         constexpr uint64_t kTileStep = kTileBytes >> 4;
-        const uint64_t qd = sw128_desc(smem_u32(sQ + w * kTileBytes), 16, 1024);
+        const uint64_t qd = sw128_desc(smem_u32(sQ), 16, 1024);
         const uint64_t kd0 = sw128_desc(smem_u32(sK), 16, 1024);
         const uint64_t vd0 = sw128_desc(smem_u32(sV), kTileBytes, 1024);
         const uint32_t d_s = tmem_base + kTmemS + w * 128;
@@ -214,61 +214,54 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int k = 0; k < kHeadDim / 16; ++k)
             umma_f16_ss(d_s, qd + 2 * k, kd + 2 * k, IDESC_S, k > 0 ? 1u : 0u);
         };
-        auto issue_pv = [&](int st, int j) {
+        auto issue_pv = [&](int st, bool first) {
           const uint64_t vd = vd0 + st * kTileStep;
 #pragma unroll
           for (int k = 0; k < kKvBlock / 16; ++k)
-            umma_f16_ts(d_o, a_p + k * 8, vd + 128 * k, IDESC_PV, (j > 0 || k > 0) ? 1u : 0u);
+            umma_f16_ts(d_o, a_p + k * 8, vd + 128 * k, IDESC_PV, (!first || k > 0) ? 1u : 0u);
         };
-        ok = mbar_wait(&k_full[0], 0, abort_flag, err, kErrAttnMma);
-        if (ok) {
-          tc_fence_after();
-          if (nbw > 0) {
-            issue_s(0);
+        {
+          const int j = w;
+          ok = mbar_wait(&k_full[j % kKvStages], static_cast<uint32_t>(j / kKvStages) & 1u, abort_flag, err,
+                         kErrAttnMma);
+          if (ok) {
+            tc_fence_after();
+            issue_s(j % kKvStages);
             umma_commit(&s_full[w]);
-            umma_commit(&k_empty[0]);
-          } else {
-            mbar_arrive(&k_empty[0]);
+            umma_commit(&k_empty[j % kKvStages]);
           }
         }
-        for (int j = 0; j < nb && ok; ++j) {
-          const int st = j % kKvStages;
-          const uint32_t ph = static_cast<uint32_t>(j / kKvStages) & 1u;
-          if (j + 1 < nb) {
-            const int st1 = (j + 1) % kKvStages;
-            const uint32_t ph1 = static_cast<uint32_t>((j + 1) / kKvStages) & 1u;
-            if (!mbar_wait(&k_full[st1], ph1, abort_flag, err, kErrAttnMma)) { ok = false; break; }
-            if (j + 1 < nbw) {
-              if (!mbar_wait(&s_free[w], static_cast<uint32_t>(j) & 1u, abort_flag, err, kErrAttnMma)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              issue_s(st1);
-              umma_commit(&s_full[w]);
-              umma_commit(&k_empty[st1]);
-            } else {
-              mbar_arrive(&k_empty[st1]);
-            }
-          }
-          if (!mbar_wait(&v_full[st], ph, abort_flag, err, kErrAttnMma)) { ok = false; break; }
-          if (j < nbw) {
-            if (!mbar_wait(&p_ready[w], static_cast<uint32_t>(j) & 1u, abort_flag, err, kErrAttnMma)) {
+        for (int i = 0; i < nbw && ok; ++i) {
+          const int j = w + 2 * i;
+          const uint32_t ipar = static_cast<uint32_t>(i) & 1u;
+          if (i + 1 < nbw) {
+            const int jn = j + 2;
+            const int stn = jn % kKvStages;
+            if (!mbar_wait(&k_full[stn], static_cast<uint32_t>(jn / kKvStages) & 1u, abort_flag, err, kErrAttnMma)) {
               ok = false;
               break;
             }
+            if (!mbar_wait(&s_free[w], ipar, abort_flag, err, kErrAttnMma)) { ok = false; break; }
             tc_fence_after();
-            issue_pv(st, j);
-            umma_commit(&o_full[w]);
-            umma_commit(&v_empty[st]);
-          } else {
-            mbar_arrive(&v_empty[st]);
+            issue_s(stn);
+            umma_commit(&s_full[w]);
+            umma_commit(&k_empty[stn]);
           }
+          const int st = j % kKvStages;
+          if (!mbar_wait(&v_full[st], static_cast<uint32_t>(j / kKvStages) & 1u, abort_flag, err, kErrAttnMma)) {
+            ok = false;
+            break;
+          }
+          if (!mbar_wait(&p_ready[w], ipar, abort_flag, err, kErrAttnMma)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(st, i == 0);
+          umma_commit(&o_full[w]);
+          umma_commit(&v_empty[st]);
         }
       }
       if (!ok) {
-        umma_commit(drain_bar + w);
-        mbar_drain_wait(drain_bar + w, 0, 1000000000ull);
+        umma_commit(&drain_bar[w]);
+        mbar_drain_wait(&drain_bar[w], 0, 1000000000ull);
       }
     }
   } else if (warp == 11) {
@@ -276,16 +269,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else {
     reg_alloc<kSoftmaxRegs>();
     // ------------------------------------------------------------- softmax --
-    // Thread = one query row. O accumulates in TMEM (the PV MMA adds onto it);
-    // the running maximum is only raised when a row's maximum grows by more
-    // than 2^kRescaleLog2, and O is rescaled in TMEM only then (P values up to
-    // 2^kRescaleLog2 are exact enough in fp16/bf16 and the sum is fp32).
+    // Thread = one query row of the tile; warpgroup w holds the online-softmax
+    // state (running max m, sum l, O_w in TMEM) of that row over its half of
+    // the key blocks. The two halves are merged at the end.
     const int w = warp >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const int qrow = q0 + w * kQTile + r;
-    const int q_first = q0 + w * kQTile;
-    const int my_nb = w ? nb1 : nb0;
+    const int qrow = q0 + r;
+    const int my_nb = w ? nb_h1 : nb_h0;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tS = tmem_base + lane_off + kTmemS + w * 128;
     const uint32_t tO = tmem_base + lane_off + kTmemO + w * kHeadDim;
@@ -294,8 +285,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
 
-    for (int j = 0; j < my_nb; ++j) {
-      if (!mbar_wait(&s_full[w], static_cast<uint32_t>(j) & 1u, abort_flag, err, kErrAttnSoftmax)) {
+    for (int i = 0; i < my_nb; ++i) {
+      const int j = w + 2 * i;
+      if (!mbar_wait(&s_full[w], static_cast<uint32_t>(i) & 1u, abort_flag, err, kErrAttnSoftmax)) {
         ok = false;
         break;
       }
@@ -312,15 +304,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_before();
       mbar_arrive(&s_free[w]);
       const int kv0 = j * kKvBlock;
-      if ((kv0 + kKvBlock > p.Skv) || (p.causal && kv0 + kKvBlock - 1 > q_first)) {
+      if ((kv0 + kKvBlock > p.Skv) || (p.causal && kv0 + kKvBlock - 1 > q0)) {
         // Keep key columns < Skv and (causal) <= this query row.
         int lim = p.Skv - kv0;
         if (p.causal && qrow - kv0 + 1 < lim) lim = qrow - kv0 + 1;
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c * 32 + i >= lim) sc[c][i] = __float_as_uint(-INFINITY);
+          for (int e = 0; e < 32; ++e)
+            if (c * 32 + e >= lim) sc[c][e] = __float_as_uint(-INFINITY);
       }
       // Row maximum: three-input max, eight independent partial maxima.
       float mxp[8];
@@ -329,8 +321,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; i += 2)
-          mxp[(i >> 1) & 7] = fmax3(mxp[(i >> 1) & 7], __uint_as_float(sc[c][i]), __uint_as_float(sc[c][i + 1]));
+        for (int e = 0; e < 32; e += 2)
+          mxp[(e >> 1) & 7] = fmax3(mxp[(e >> 1) & 7], __uint_as_float(sc[c][e]), __uint_as_float(sc[c][e + 1]));
       const float mx = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7]));
       const float m_cand = mx * sl2;
       // Running maximum: raised only when a row's maximum grows by more than
@@ -338,7 +330,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // previous block's P V has landed.
       bool rescale = false;
       float alpha = 1.f;
-      if (j == 0) {
+      if (i == 0) {
         m_used = m_cand;
       } else if (__any_sync(0xffffffffu, m_cand > m_used + kRescaleLog2)) {
         const float m_next = fmaxf(m_used, m_cand);
@@ -377,8 +369,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       l += ls.x + ls.y;
       // The previous block's P V must be complete (P_w consumed, O_w updated)
       // before P_w is overwritten and O_w is rescaled; by now it normally is.
-      if (j > 0) {
-        if (!mbar_wait(&o_full[w], static_cast<uint32_t>(j - 1) & 1u, abort_flag, err, kErrAttnSoftmax)) {
+      if (i > 0) {
+        if (!mbar_wait(&o_full[w], static_cast<uint32_t>(i - 1) & 1u, abort_flag, err, kErrAttnSoftmax)) {
           ok = false;
           break;
         }
@@ -406,28 +398,54 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_before();
       mbar_arrive(&p_ready[w]);
     }
+    // ------------------------------------------------------------ merge --
+    // Publish this half's (m, l) after its last P V has landed, wait for the
+    // other half, then warpgroup w writes output columns [32w, 32w + 32) of
+    // the row: O = (O_0 2^(m_0 - m) + O_1 2^(m_1 - m)) / (l_0 2^(m_0 - m) + l_1 2^(m_1 - m)).
     if (ok && my_nb > 0) {
-      if (mbar_wait(&o_full[w], static_cast<uint32_t>(my_nb - 1) & 1u, abort_flag, err, kErrAttnSoftmax)) {
-        tc_fence_after();
-        const float inv_l = 1.0f / l;
-        T* out = static_cast<T*>(p.O) + b * p.os_b + h * p.os_h + static_cast<int64_t>(qrow) * p.os_s;
+      ok = mbar_wait(&o_full[w], static_cast<uint32_t>(my_nb - 1) & 1u, abort_flag, err, kErrAttnSoftmax);
+    }
+    if (ok) {
+      s_stats[(w * 2 + 0) * kQTile + r] = m_used;
+      s_stats[(w * 2 + 1) * kQTile + r] = l;
+      tc_fence_before();
+      mbar_arrive(stats_ready);
+      ok = mbar_wait(stats_ready, 0, abort_flag, err, kErrAttnSoftmax);
+    }
+    if (ok) {
+      tc_fence_after();
+      const float m0 = s_stats[0 * kQTile + r], l0 = s_stats[1 * kQTile + r];
+      const float m1 = s_stats[2 * kQTile + r], l1 = s_stats[3 * kQTile + r];
+      const bool has0 = nb_h0 > 0, has1 = nb_h1 > 0;
+      const float m = fmaxf(has0 ? m0 : -INFINITY, has1 ? m1 : -INFINITY);
+      const float a0 = (has0 && m0 != -INFINITY) ? ex2_approx(m0 - m) : 0.f;
+      const float a1 = (has1 && m1 != -INFINITY) ? ex2_approx(m1 - m) : 0.f;
+      const float inv_l = 1.0f / (l0 * a0 + l1 * a1);
+      const float c0 = a0 * inv_l, c1 = a1 * inv_l;
+      const uint32_t col = static_cast<uint32_t>(w * 32);
+      uint32_t o0[32], o1[32];
+      if (has0) tmem_ld_32x32b_x32(tmem_base + lane_off + kTmemO + col, o0);
+      if (has1) tmem_ld_32x32b_x32(tmem_base + lane_off + kTmemO + kHeadDim + col, o1);
+      tmem_ld_wait_regs(o0);
+      reg_fence(o1);
+      if (qrow < p.Sq) {
+        T* out = static_cast<T*>(p.O) + b * p.os_b + h * p.os_h + static_cast<int64_t>(qrow) * p.os_s + col;
         uint4* ov4 = reinterpret_cast<uint4*>(out);
 #pragma unroll
-        for (int c = 0; c < kHeadDim / 32; ++c) {
-          uint32_t ov[32];
-          tmem_ld_32x32b_x32(tO + c * 32, ov);
-          tmem_ld_wait_regs(ov);
-          if (qrow < p.Sq) {
+        for (int q = 0; q < 4; ++q) {
+          float f[8];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 u;
-              u.x = Io<T>::pack2(__uint_as_float(ov[8 * q + 0]) * inv_l, __uint_as_float(ov[8 * q + 1]) * inv_l);
-              u.y = Io<T>::pack2(__uint_as_float(ov[8 * q + 2]) * inv_l, __uint_as_float(ov[8 * q + 3]) * inv_l);
-              u.z = Io<T>::pack2(__uint_as_float(ov[8 * q + 4]) * inv_l, __uint_as_float(ov[8 * q + 5]) * inv_l);
-              u.w = Io<T>::pack2(__uint_as_float(ov[8 * q + 6]) * inv_l, __uint_as_float(ov[8 * q + 7]) * inv_l);
-              ov4[c * 4 + q] = u;
-            }
+          for (int e = 0; e < 8; ++e) {
+            const float v0 = has0 ? __uint_as_float(o0[8 * q + e]) * c0 : 0.f;
+            const float v1 = has1 ? __uint_as_float(o1[8 * q + e]) * c1 : 0.f;
+            f[e] = v0 + v1;
           }
+          uint4 u;
+          u.x = Io<T>::pack2(f[0], f[1]);
+          u.y = Io<T>::pack2(f[2], f[3]);
+          u.z = Io<T>::pack2(f[4], f[5]);
+          u.w = Io<T>::pack2(f[6], f[7]);
+          ov4[q] = u;
         }
       }
     }
@@ -543,12 +561,12 @@ cudaError_t run_tc(const AttnArgs& a, cudaStream_t s) {
   p.H = static_cast<int>(a.H);
   p.Sq = static_cast<int>(a.Sq);
   p.Skv = static_cast<int>(a.Skv);
-  p.n_qblocks = static_cast<int>(ceil_div64(a.Sq, 2 * kQTile));
+  p.n_qtiles = static_cast<int>(ceil_div64(a.Sq, kQTile));
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.causal = a.causal;
   unsigned int* err = device_error_word();
   if (err == nullptr) return cudaErrorInvalidDevice;
-  const dim3 grid(static_cast<unsigned>(p.n_qblocks), static_cast<unsigned>(a.H), static_cast<unsigned>(a.B));
+  const dim3 grid(static_cast<unsigned>(p.n_qtiles), static_cast<unsigned>(a.H), static_cast<unsigned>(a.B));
   return launch_pdl(kern, grid, dim3(kAttnThreads), static_cast<size_t>(kAttnSmem), s, mq, mk, mv, p, err);
 }
 
