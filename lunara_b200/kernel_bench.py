@@ -7,8 +7,9 @@
   bias_gelu         16384 x 3072 fp16 + bias, tanh GELU   (201.33 MB moved)
   stack             12-layer encoder stack, batch 64 split over the ranks
 
-Each step is one launch (or one stack forward) bracketed by CUDA events, with
-a 256 MB L2-flush write between steps outside the events. Used by bench.py.
+Each step replays a CUDA graph of 10 back-to-back launches (the stack: one
+forward) between CUDA events, with a 256 MB L2-flush write between steps
+outside the events; the per-launch time is the step time / 10. Used by bench.py.
 """
 from __future__ import annotations
 
@@ -29,21 +30,31 @@ def _peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def _time_steps(fn, steps, warmup, flush):
+def _time_steps(fn, steps, warmup, flush, reps=10):
+    """Per-launch device time of ``fn`` (ms), one value per step.
+
+    ``fn`` is captured REPS times into one CUDA graph; a step replays the
+    graph between CUDA events, after a 256 MB L2-flush write outside them, and
+    counts time / REPS, so host launch cost is not in the number (the first
+    launch of a step reads cold L2, the others warm).
+    """
+    from lunara_b200.runtime.encoder import GraphRunner
+    runner = GraphRunner(lambda: [fn() for _ in range(reps)])
     stream = torch.cuda.current_stream()
     for _ in range(warmup):
         flush.zero_()
-        fn()
+        runner.replay()
     torch.cuda.synchronize()
     times = []
     for _ in range(steps):
         flush.zero_()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(stream)
-        fn()
+        runner.replay()
         e.record(stream)
         e.synchronize()
-        times.append(s.elapsed_time(e))
+        times.append(s.elapsed_time(e) / reps)
+    runner.release()
     return times
 
 
@@ -104,21 +115,19 @@ def run(workload, args, rank, world, device):
                     roofline={"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                               "peak_source": f"{src} copy"})
     elif workload == "stack":
-        from lunara_b200.runtime.encoder import EncoderStack, GraphRunner
+        from lunara_b200.runtime.encoder import EncoderStack
         per_rank = 64 // world
         x, ws = inputs.stack_inputs(batch=64, seq=512, layers=12, seed=4)
         xs = x[rank * per_rank:(rank + 1) * per_rank]
         st = EncoderStack(ws, batch=per_rank, seq=512, num_heads=12, device=device)
         st.x.copy_(xs.half().reshape(-1, 768).to(device))
-        runner = GraphRunner(st.run_kernels)
-        t = _time_steps(runner.replay, args.steps, args.warmup, flush)
+        t = _time_steps(st.run_kernels, args.steps, args.warmup, flush, reps=1)
         total = sum(t)
         if world > 1:
             import torch.distributed as dist
             tt = torch.tensor([total], dtype=torch.float64, device=device)
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             total = float(tt.item())
-        runner.release()
         tokens = 64 * 512 * args.steps
         val = tokens / (total * 1e-3)
         flops = 12 * 8 * 64.42e9 * args.steps
