@@ -1,16 +1,18 @@
 // Scaled-dot-product attention forward, O = softmax(Q K^T * scale [+ causal]) V.
 //
 // tcgen05 path (f16 / bf16, D == 64): FlashAttention-style single pass with an
-// online softmax. One CTA owns one 128-row Q tile of one (batch, head); its two
-// halves split the key blocks (half 0 takes blocks 0, 2, 4, ..., half 1 takes
-// 1, 3, 5, ...), each keeping its own running max, row sum and O, and merge
-// them at the end. One tile per CTA gives twice as many CTAs as tile pairs
-// would, which evens out the last wave on 148 SMs.
+// online softmax. A persistent CTA (one per SM) works through 128-row Q tiles
+// of (batch, head) pairs; for each tile its two halves split the key blocks
+// (half 0 takes blocks 0, 2, 4, ..., half 1 takes 1, 3, 5, ...), each keeping
+// its own running max, row sum and O, and merge them at the end. Tile-sized
+// work items even out the last round on 148 SMs, and persistence pays the
+// set-up (TMEM allocation, barriers, first loads) once per SM: the next
+// tile's Q and key blocks load while the current tile finishes.
 //   warps 0-3   softmax warpgroup 0 (thread = query row), half 0
 //   warps 4-7   softmax warpgroup 1 (same rows), half 1
-//   warp 8      TMA producer: the Q tile once, K and V [128 x 64] blocks into a
-//               4-deep ring (128-byte swizzle, 4-D tensor maps over the
-//               caller's strides, so a fused QKV buffer is read in place)
+//   warp 8      TMA producer: Q tiles into a 2-deep buffer, K and V [128 x 64]
+//               blocks into a 4-deep ring (128-byte swizzle, 4-D tensor maps
+//               over the caller's strides, so a fused QKV buffer is read in place)
 //   warps 9-10  tcgen05.mma issuers, one per half (warp 9 also allocates TMEM)
 //                 S_w = Q K_j^T     (M=128, N=128, K=64; A, B from shared memory)
 //                 O_w += P_w V_j    (M=128, N=64, K=128; A = P_w from TMEM)
@@ -59,7 +61,7 @@ constexpr float kRescaleLog2 = 8.0f;
 constexpr int kPolyPairs = LUNARA_ATTN_POLY_PAIRS;
 static_assert(kPolyPairs >= 0 && kPolyPairs <= 16, "poly pairs per chunk");
 constexpr uint32_t kTileBytes = 128 * 128;  // one [128 x 64] 16-bit tile
-constexpr int kAttnSmem = kTileBytes + 2 * kKvStages * kTileBytes + 4 * kQTile * 4 + 256 + 1024;
+constexpr int kAttnSmem = 2 * kTileBytes + 2 * kKvStages * kTileBytes + 4 * kQTile * 4 + 512 + 1024;
 // TMEM columns: S_w (128 fp32 columns per Q tile), O_w (64), P_w (128 16-bit
 // values packed in 64 columns).
 constexpr uint32_t kTmemS = 0;
@@ -70,11 +72,42 @@ constexpr uint32_t kAttnTmemCols = 512;
 struct AttnParams {
   void* O;
   int64_t os_b, os_h, os_s;
-  int H, Sq, Skv;
+  int B, H, Sq, Skv;
   int n_qtiles;
   float scale_log2;
   int causal;
 };
+
+// Work item of a persistent CTA: one 128-row Q tile of one (batch, head).
+// Tiles are numbered with the query-tile index outermost (for causal
+// attention, heaviest first); CTA c takes tiles c, 2G-1-c, 2G+c, 4G-1-c, ...
+// (a snake over rounds of G = gridDim.x tiles), which pairs heavy and light
+// causal tiles on the same CTA.
+struct AttnTile {
+  int q0, h, b, nb;
+};
+
+__device__ __forceinline__ int attn_tile_index(int k, int c, int G) {
+  return k * G + ((k & 1) ? (G - 1 - c) : c);
+}
+
+__device__ __forceinline__ AttnTile attn_tile(int t, const AttnParams& p) {
+  const int hb_count = p.H * p.B;
+  const int qi = t / hb_count;
+  const int hb = t - qi * hb_count;
+  AttnTile x;
+  const int qt = p.causal ? (p.n_qtiles - 1 - qi) : qi;
+  x.q0 = qt * kQTile;
+  x.h = hb % p.H;
+  x.b = hb / p.H;
+  const int nb_total = (p.Skv + kKvBlock - 1) / kKvBlock;
+  x.nb = nb_total;
+  if (p.causal) {
+    const int lim = (x.q0 + kQTile - 1) / kKvBlock + 1;
+    x.nb = lim < nb_total ? lim : nb_total;
+  }
+  return x;
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -86,13 +119,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
-  uint8_t* sQ = smem;                                   // the Q tile
-  uint8_t* sK = sQ + kTileBytes;                        // kKvStages tiles
+  uint8_t* sQ = smem;                                   // 2 Q tiles (double buffer over work items)
+  uint8_t* sK = sQ + 2 * kTileBytes;                    // kKvStages tiles
   uint8_t* sV = sK + kKvStages * kTileBytes;            // kKvStages tiles
   float* s_stats = reinterpret_cast<float*>(sV + kKvStages * kTileBytes);   // [half][m | l][row]
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_stats + 2 * 2 * kQTile);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
+  uint64_t* q_full = bars;                  // [2]
+  uint64_t* q_empty = q_full + 2;           // [2] both issuers done with the Q buffer
+  uint64_t* k_full = q_empty + 2;
   uint64_t* k_empty = k_full + kKvStages;
   uint64_t* v_full = k_empty + kKvStages;
   uint64_t* v_empty = v_full + kKvStages;
@@ -100,29 +134,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* s_free = s_full + 2;            // [2] S_w read into registers (buffer reusable)
   uint64_t* p_ready = s_free + 2;           // [2] P_w written to TMEM
   uint64_t* o_full = p_ready + 2;           // [2] P_w V done (O_w updated, P_w consumed)
-  uint64_t* stats_ready = o_full + 2;       // both halves' O, m, l final
-  uint64_t* drain_bar = stats_ready + 1;    // [2] one per MMA issuer
+  uint64_t* stats_ready = o_full + 2;       // both halves' O, m, l of the work item final
+  uint64_t* o_free = stats_ready + 1;       // the merge has read both O buffers
+  uint64_t* drain_bar = o_free + 1;         // [2] one per MMA issuer
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int qt = p.causal ? (p.n_qtiles - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
-  const int q0 = qt * kQTile;
-  // Key blocks of this Q tile: 0 .. nb-1 (causal: up to the diagonal block).
-  // Half w of the CTA (softmax warpgroup w and MMA warp 9+w) takes blocks j = w, w+2, ...
-  const int nb_total = (p.Skv + kKvBlock - 1) / kKvBlock;
-  int nb = nb_total;
-  if (p.causal) {
-    const int lim = (q0 + kQTile - 1) / kKvBlock + 1;
-    nb = lim < nb_total ? lim : nb_total;
-  }
-  const int nb_h0 = (nb + 1) / 2, nb_h1 = nb / 2;   // blocks of half 0 / half 1
+  const int G = static_cast<int>(gridDim.x);
+  const int cta = static_cast<int>(blockIdx.x);
+  const int n_tiles = p.n_qtiles * p.H * p.B;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 2);
+    }
     for (int s = 0; s < kKvStages; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -137,6 +165,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&drain_bar[w], 1);
     }
     mbar_init(stats_ready, 2 * kQTile);
+    mbar_init(o_free, 2 * kQTile);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -156,28 +185,43 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     reg_dealloc<kProducerRegs>();
     if (lane == 0) {
       // -------------------------------------------------------- TMA producer --
+      // Per work item: its Q tile into the free Q buffer, then its key blocks
+      // into the K/V ring (ring slots and phases count blocks across items).
       tma_prefetch_desc(&tq);
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
-      mbar_arrive_expect_tx(q_full, kTileBytes);
-      tma_load_4d(sQ, &tq, q_full, 0, q0, h, b);
-      int issued_k = 0, issued_v = 0;
+      int issued_q = 0, issued_kv = 0, issued_v = 0;
       bool ok = true;
-      for (int j = 0; j < nb && ok; ++j) {
-        const int st = j % kKvStages;
-        const uint32_t ph = static_cast<uint32_t>(j / kKvStages) & 1u;
-        if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, err, kErrAttnProducer)) { ok = false; break; }
-        mbar_arrive_expect_tx(&k_full[st], kTileBytes);
-        tma_load_4d(sK + st * kTileBytes, &tk, &k_full[st], 0, j * kKvBlock, h, b);
-        ++issued_k;
-        if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, err, kErrAttnProducer)) { ok = false; break; }
-        mbar_arrive_expect_tx(&v_full[st], kTileBytes);
-        tma_load_4d(sV + st * kTileBytes, &tv, &v_full[st], 0, j * kKvBlock, h, b);
-        ++issued_v;
+      for (int k = 0; ok; ++k) {
+        const int t = attn_tile_index(k, cta, G);
+        if (t >= n_tiles) break;
+        const AttnTile x = attn_tile(t, p);
+        const int buf = k & 1;
+        if (!mbar_wait(&q_empty[buf], (static_cast<uint32_t>(k >> 1) & 1u) ^ 1u, abort_flag, err, kErrAttnProducer)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&q_full[buf], kTileBytes);
+        tma_load_4d(sQ + buf * kTileBytes, &tq, &q_full[buf], 0, x.q0, x.h, x.b);
+        ++issued_q;
+        for (int j = 0; j < x.nb; ++j) {
+          const int g = issued_kv;
+          const int st = g % kKvStages;
+          const uint32_t ph = static_cast<uint32_t>(g / kKvStages) & 1u;
+          if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, err, kErrAttnProducer)) { ok = false; break; }
+          mbar_arrive_expect_tx(&k_full[st], kTileBytes);
+          tma_load_4d(sK + st * kTileBytes, &tk, &k_full[st], 0, j * kKvBlock, x.h, x.b);
+          ++issued_kv;
+          if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, err, kErrAttnProducer)) { ok = false; break; }
+          mbar_arrive_expect_tx(&v_full[st], kTileBytes);
+          tma_load_4d(sV + st * kTileBytes, &tv, &v_full[st], 0, j * kKvBlock, x.h, x.b);
+          ++issued_v;
+        }
       }
       if (!ok) {
-        mbar_drain_wait(q_full, 0, 1000000000ull);
-        for (int i = (issued_k > kKvStages ? issued_k - kKvStages : 0); i < issued_k; ++i)
+        for (int i = (issued_q > 2 ? issued_q - 2 : 0); i < issued_q; ++i)
+          mbar_drain_wait(&q_full[i & 1], static_cast<uint32_t>(i >> 1) & 1u, 1000000000ull);
+        for (int i = (issued_kv > kKvStages ? issued_kv - kKvStages : 0); i < issued_kv; ++i)
           mbar_drain_wait(&k_full[i % kKvStages], static_cast<uint32_t>(i / kKvStages) & 1u, 1000000000ull);
         for (int i = (issued_v > kKvStages ? issued_v - kKvStages : 0); i < issued_v; ++i)
           mbar_drain_wait(&v_full[i % kKvStages], static_cast<uint32_t>(i / kKvStages) & 1u, 1000000000ull);
@@ -187,77 +231,110 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     reg_dealloc<kProducerRegs>();
     if (lane == 0) {
       // ------------------------------------------------------ MMA issuers --
-      // Warp 9 + w issues the MMAs of half w, for its key blocks j = w + 2i:
-      // S_w(next) as soon as the softmax has pulled S_w(j) into registers (the
-      // next scores are ready when it finishes block j), then P_w(j) V_j once
-      // P_w(j) is in TMEM. Each ring stage holds one key block and is released
-      // by the issuer of the half that uses it.
+      // Warp 9 + w issues the MMAs of half w, for its key blocks j = w + 2i of
+      // each work item: S_w(next) as soon as the softmax has pulled the current
+      // S_w into registers (the next scores are ready when it finishes the
+      // current block), then P_w V_j once P_w is in TMEM. A ring stage holds
+      // one key block and is released by the issuer of the half that uses it;
+      // a Q buffer is released by both issuers after their last S of the item.
       const int w = warp - 9;
-      const int nbw = w ? nb_h1 : nb_h0;
-      bool ok = mbar_wait(q_full, 0, abort_flag, err, kErrAttnMma);
-      if (ok && nbw > 0) {
-        tc_fence_after();
-        // Descriptors are built once; the start-address field (bits 0-13, in
-        // 16-byte units) then moves by constants: +32 B per K step within a
-        // K-major row (Q, K), +2048 B (16 rows of 128 B) per K step down V,
-        // and one tile (16 KB) per ring stage.
-        constexpr uint64_t kTileStep = kTileBytes >> 4;
-        const uint64_t qd = sw128_desc(smem_u32(sQ), 16, 1024);
-        const uint64_t kd0 = sw128_desc(smem_u32(sK), 16, 1024);
-        const uint64_t vd0 = sw128_desc(smem_u32(sV), kTileBytes, 1024);
-        const uint32_t d_s = tmem_base + kTmemS + w * 128;
-        const uint32_t d_o = tmem_base + kTmemO + w * kHeadDim;
-        const uint32_t a_p = tmem_base + kTmemP + w * (kKvBlock / 2);
-        auto issue_s = [&](int st) {
-          const uint64_t kd = kd0 + st * kTileStep;
+      constexpr uint64_t kTileStep = kTileBytes >> 4;
+      // Descriptors are built once; the start-address field (bits 0-13, in
+      // 16-byte units) then moves by constants: +32 B per K step within a
+      // K-major row (Q, K), +2048 B (16 rows of 128 B) per K step down V, and
+      // one tile (16 KB) per Q buffer or ring stage.
+      const uint64_t qd0 = sw128_desc(smem_u32(sQ), 16, 1024);
+      const uint64_t kd0 = sw128_desc(smem_u32(sK), 16, 1024);
+      const uint64_t vd0 = sw128_desc(smem_u32(sV), kTileBytes, 1024);
+      const uint32_t d_s = tmem_base + kTmemS + w * 128;
+      const uint32_t d_o = tmem_base + kTmemO + w * kHeadDim;
+      const uint32_t a_p = tmem_base + kTmemP + w * (kKvBlock / 2);
+      auto issue_s = [&](uint64_t qd, int st) {
+        const uint64_t kd = kd0 + st * kTileStep;
 #pragma unroll
-          for (int k = 0; k < kHeadDim / 16; ++k)
-            umma_f16_ss(d_s, qd + 2 * k, kd + 2 * k, IDESC_S, k > 0 ? 1u : 0u);
-        };
-        auto issue_pv = [&](int st, bool first) {
-          const uint64_t vd = vd0 + st * kTileStep;
+        for (int kk = 0; kk < kHeadDim / 16; ++kk)
+          umma_f16_ss(d_s, qd + 2 * kk, kd + 2 * kk, IDESC_S, kk > 0 ? 1u : 0u);
+      };
+      auto issue_pv = [&](int st, bool first) {
+        const uint64_t vd = vd0 + st * kTileStep;
 #pragma unroll
-          for (int k = 0; k < kKvBlock / 16; ++k)
-            umma_f16_ts(d_o, a_p + k * 8, vd + 128 * k, IDESC_PV, (!first || k > 0) ? 1u : 0u);
-        };
-        {
-          const int j = w;
-          ok = mbar_wait(&k_full[j % kKvStages], static_cast<uint32_t>(j / kKvStages) & 1u, abort_flag, err,
-                         kErrAttnMma);
-          if (ok) {
-            tc_fence_after();
-            issue_s(j % kKvStages);
-            umma_commit(&s_full[w]);
-            umma_commit(&k_empty[j % kKvStages]);
-          }
+        for (int kk = 0; kk < kKvBlock / 16; ++kk)
+          umma_f16_ts(d_o, a_p + kk * 8, vd + 128 * kk, IDESC_PV, (!first || kk > 0) ? 1u : 0u);
+      };
+      bool ok = true;
+      int gi = 0;        // this half's blocks so far (phase of s_full / s_free / p_ready / o_full)
+      int gb_base = 0;   // ring index of the current item's block 0
+      for (int k = 0; ok; ++k) {
+        const int t = attn_tile_index(k, cta, G);
+        if (t >= n_tiles) break;
+        const AttnTile x = attn_tile(t, p);
+        const int nbw = w ? x.nb / 2 : (x.nb + 1) / 2;
+        const int buf = k & 1;
+        if (!mbar_wait(&q_full[buf], static_cast<uint32_t>(k >> 1) & 1u, abort_flag, err, kErrAttnMma)) {
+          ok = false;
+          break;
         }
-        for (int i = 0; i < nbw && ok; ++i) {
-          const int j = w + 2 * i;
-          const uint32_t ipar = static_cast<uint32_t>(i) & 1u;
-          if (i + 1 < nbw) {
-            const int jn = j + 2;
-            const int stn = jn % kKvStages;
-            if (!mbar_wait(&k_full[stn], static_cast<uint32_t>(jn / kKvStages) & 1u, abort_flag, err, kErrAttnMma)) {
-              ok = false;
-              break;
-            }
-            if (!mbar_wait(&s_free[w], ipar, abort_flag, err, kErrAttnMma)) { ok = false; break; }
-            tc_fence_after();
-            issue_s(stn);
-            umma_commit(&s_full[w]);
-            umma_commit(&k_empty[stn]);
-          }
-          const int st = j % kKvStages;
-          if (!mbar_wait(&v_full[st], static_cast<uint32_t>(j / kKvStages) & 1u, abort_flag, err, kErrAttnMma)) {
+        if (nbw == 0) {
+          mbar_arrive(&q_empty[buf]);
+          gb_base += x.nb;
+          continue;
+        }
+        tc_fence_after();
+        const uint64_t qd = qd0 + buf * kTileStep;
+        {
+          const int g = gb_base + w;
+          if (!mbar_wait(&k_full[g % kKvStages], static_cast<uint32_t>(g / kKvStages) & 1u, abort_flag, err,
+                         kErrAttnMma)) {
             ok = false;
             break;
           }
-          if (!mbar_wait(&p_ready[w], ipar, abort_flag, err, kErrAttnMma)) { ok = false; break; }
+          if (gi > 0 && !mbar_wait(&s_free[w], static_cast<uint32_t>(gi - 1) & 1u, abort_flag, err, kErrAttnMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s(qd, g % kKvStages);
+          umma_commit(&s_full[w]);
+          umma_commit(&k_empty[g % kKvStages]);
+          if (nbw == 1) umma_commit(&q_empty[buf]);
+        }
+        for (int i = 0; i < nbw && ok; ++i) {
+          const int g = gb_base + w + 2 * i;
+          const uint32_t cpar = static_cast<uint32_t>(gi + i) & 1u;
+          if (i + 1 < nbw) {
+            const int gn = g + 2;
+            if (!mbar_wait(&k_full[gn % kKvStages], static_cast<uint32_t>(gn / kKvStages) & 1u, abort_flag, err,
+                           kErrAttnMma)) {
+              ok = false;
+              break;
+            }
+            if (!mbar_wait(&s_free[w], cpar, abort_flag, err, kErrAttnMma)) { ok = false; break; }
+            tc_fence_after();
+            issue_s(qd, gn % kKvStages);
+            umma_commit(&s_full[w]);
+            umma_commit(&k_empty[gn % kKvStages]);
+            if (i + 2 == nbw) umma_commit(&q_empty[buf]);
+          }
+          const int st = g % kKvStages;
+          if (!mbar_wait(&v_full[st], static_cast<uint32_t>(g / kKvStages) & 1u, abort_flag, err, kErrAttnMma)) {
+            ok = false;
+            break;
+          }
+          if (!mbar_wait(&p_ready[w], cpar, abort_flag, err, kErrAttnMma)) { ok = false; break; }
+          // The first P V of an item overwrites O_w: the previous item's merge
+          // must have read it.
+          if (i == 0 && k > 0 &&
+              !mbar_wait(o_free, static_cast<uint32_t>(k - 1) & 1u, abort_flag, err, kErrAttnMma)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           issue_pv(st, i == 0);
           umma_commit(&o_full[w]);
           umma_commit(&v_empty[st]);
         }
+        gi += nbw;
+        gb_base += x.nb;
       }
       if (!ok) {
         umma_commit(&drain_bar[w]);
@@ -269,25 +346,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else {
     reg_alloc<kSoftmaxRegs>();
     // ------------------------------------------------------------- softmax --
-    // Thread = one query row of the tile; warpgroup w holds the online-softmax
-    // state (running max m, sum l, O_w in TMEM) of that row over its half of
-    // the key blocks. The two halves are merged at the end.
+    // Thread = one query row of the work item; warpgroup w holds the online-
+    // softmax state (running max m, sum l, O_w in TMEM) of that row over its
+    // half of the key blocks. The two halves are merged at the end of the item.
     const int w = warp >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const int qrow = q0 + r;
-    const int my_nb = w ? nb_h1 : nb_h0;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tS = tmem_base + lane_off + kTmemS + w * 128;
     const uint32_t tO = tmem_base + lane_off + kTmemO + w * kHeadDim;
     const uint32_t tP = tmem_base + lane_off + kTmemP + w * (kKvBlock / 2);
     const float sl2 = p.scale_log2;
-    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
+    int gi = 0;   // this half's blocks so far (barrier phases)
+    for (int k = 0; ok; ++k) {
+      const int t = attn_tile_index(k, cta, G);
+      if (t >= n_tiles) break;
+      const AttnTile x = attn_tile(t, p);
+      const int q0 = x.q0;
+      const int qrow = q0 + r;
+      const int nb_h0 = (x.nb + 1) / 2, nb_h1 = x.nb / 2;
+      const int my_nb = w ? nb_h1 : nb_h0;
+      float m_used = -INFINITY, l = 0.f;
 
     for (int i = 0; i < my_nb; ++i) {
       const int j = w + 2 * i;
-      if (!mbar_wait(&s_full[w], static_cast<uint32_t>(i) & 1u, abort_flag, err, kErrAttnSoftmax)) {
+      const int cur = gi + i;
+      if (!mbar_wait(&s_full[w], static_cast<uint32_t>(cur) & 1u, abort_flag, err, kErrAttnSoftmax)) {
         ok = false;
         break;
       }
@@ -296,7 +381,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // buffer is handed back so the next block's scores can be computed.
       uint32_t sc[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tS + c * 32, sc[c]);
+      for (int cc = 0; cc < 4; ++cc) tmem_ld_32x32b_x32(tS + cc * 32, sc[cc]);
       tmem_ld_wait_regs(sc[0]);
       reg_fence(sc[1]);
       reg_fence(sc[2]);
@@ -309,20 +394,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         int lim = p.Skv - kv0;
         if (p.causal && qrow - kv0 + 1 < lim) lim = qrow - kv0 + 1;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int cc = 0; cc < 4; ++cc)
 #pragma unroll
           for (int e = 0; e < 32; ++e)
-            if (c * 32 + e >= lim) sc[c][e] = __float_as_uint(-INFINITY);
+            if (cc * 32 + e >= lim) sc[cc][e] = __float_as_uint(-INFINITY);
       }
       // Row maximum: three-input max, eight independent partial maxima.
       float mxp[8];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) mxp[t] = -INFINITY;
+      for (int tt = 0; tt < 8; ++tt) mxp[tt] = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int cc = 0; cc < 4; ++cc)
 #pragma unroll
         for (int e = 0; e < 32; e += 2)
-          mxp[(e >> 1) & 7] = fmax3(mxp[(e >> 1) & 7], __uint_as_float(sc[c][e]), __uint_as_float(sc[c][e + 1]));
+          mxp[(e >> 1) & 7] = fmax3(mxp[(e >> 1) & 7], __uint_as_float(sc[cc][e]), __uint_as_float(sc[cc][e + 1]));
       const float mx = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7]));
       const float m_cand = mx * sl2;
       // Running maximum: raised only when a row's maximum grows by more than
@@ -370,7 +455,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // The previous block's P V must be complete (P_w consumed, O_w updated)
       // before P_w is overwritten and O_w is rescaled; by now it normally is.
       if (i > 0) {
-        if (!mbar_wait(&o_full[w], static_cast<uint32_t>(i - 1) & 1u, abort_flag, err, kErrAttnSoftmax)) {
+        if (!mbar_wait(&o_full[w], static_cast<uint32_t>(cur - 1) & 1u, abort_flag, err, kErrAttnSoftmax)) {
           ok = false;
           break;
         }
@@ -398,21 +483,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_before();
       mbar_arrive(&p_ready[w]);
     }
-    // ------------------------------------------------------------ merge --
-    // Publish this half's (m, l) after its last P V has landed, wait for the
-    // other half, then warpgroup w writes output columns [32w, 32w + 32) of
-    // the row: O = (O_0 2^(m_0 - m) + O_1 2^(m_1 - m)) / (l_0 2^(m_0 - m) + l_1 2^(m_1 - m)).
-    if (ok && my_nb > 0) {
-      ok = mbar_wait(&o_full[w], static_cast<uint32_t>(my_nb - 1) & 1u, abort_flag, err, kErrAttnSoftmax);
-    }
-    if (ok) {
+      // ---------------------------------------------------------- merge --
+      // Publish this half's (m, l) once its last P V has landed, wait for the
+      // other half, then warpgroup w writes output columns [32w, 32w + 32) of
+      // the row: O = (O_0 2^(m_0 - m) + O_1 2^(m_1 - m)) / (l_0 2^(m_0 - m) + l_1 2^(m_1 - m)).
+      if (ok && my_nb > 0) {
+        ok = mbar_wait(&o_full[w], static_cast<uint32_t>(gi + my_nb - 1) & 1u, abort_flag, err, kErrAttnSoftmax);
+      }
+      if (!ok) break;
       s_stats[(w * 2 + 0) * kQTile + r] = m_used;
       s_stats[(w * 2 + 1) * kQTile + r] = l;
       tc_fence_before();
       mbar_arrive(stats_ready);
-      ok = mbar_wait(stats_ready, 0, abort_flag, err, kErrAttnSoftmax);
-    }
-    if (ok) {
+      if (!mbar_wait(stats_ready, static_cast<uint32_t>(k) & 1u, abort_flag, err, kErrAttnSoftmax)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const float m0 = s_stats[0 * kQTile + r], l0 = s_stats[1 * kQTile + r];
       const float m1 = s_stats[2 * kQTile + r], l1 = s_stats[3 * kQTile + r];
@@ -423,31 +509,39 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const float inv_l = 1.0f / (l0 * a0 + l1 * a1);
       const float c0 = a0 * inv_l, c1 = a1 * inv_l;
       const uint32_t col = static_cast<uint32_t>(w * 32);
-      uint32_t o0[32], o1[32];
-      if (has0) tmem_ld_32x32b_x32(tmem_base + lane_off + kTmemO + col, o0);
-      if (has1) tmem_ld_32x32b_x32(tmem_base + lane_off + kTmemO + kHeadDim + col, o1);
-      tmem_ld_wait_regs(o0);
-      reg_fence(o1);
-      if (qrow < p.Sq) {
-        T* out = static_cast<T*>(p.O) + b * p.os_b + h * p.os_h + static_cast<int64_t>(qrow) * p.os_s + col;
-        uint4* ov4 = reinterpret_cast<uint4*>(out);
+      T* out = static_cast<T*>(p.O) + x.b * p.os_b + x.h * p.os_h + static_cast<int64_t>(qrow) * p.os_s + col;
+      // Two rounds of 16 columns keep the merge's register footprint small.
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float f[8];
+      for (int hcol = 0; hcol < 2; ++hcol) {
+        uint32_t o0[16], o1[16];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float v0 = has0 ? __uint_as_float(o0[8 * q + e]) * c0 : 0.f;
-            const float v1 = has1 ? __uint_as_float(o1[8 * q + e]) * c1 : 0.f;
-            f[e] = v0 + v1;
+        for (int e = 0; e < 16; ++e) o0[e] = o1[e] = 0u;
+        if (has0) tmem_ld_32x32b_x16(tmem_base + lane_off + kTmemO + col + hcol * 16, o0);
+        if (has1) tmem_ld_32x32b_x16(tmem_base + lane_off + kTmemO + kHeadDim + col + hcol * 16, o1);
+        tmem_ld_wait_regs16(o0, o1);
+        if (hcol == 1) {
+          // Both O buffers read: the next item's first P V may overwrite them.
+          tc_fence_before();
+          mbar_arrive(o_free);
+        }
+        if (qrow < p.Sq) {
+          uint4* ov4 = reinterpret_cast<uint4*>(out + hcol * 16);
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              f[e] = __uint_as_float(o0[8 * q + e]) * c0 + __uint_as_float(o1[8 * q + e]) * c1;
+            uint4 u;
+            u.x = Io<T>::pack2(f[0], f[1]);
+            u.y = Io<T>::pack2(f[2], f[3]);
+            u.z = Io<T>::pack2(f[4], f[5]);
+            u.w = Io<T>::pack2(f[6], f[7]);
+            ov4[q] = u;
           }
-          uint4 u;
-          u.x = Io<T>::pack2(f[0], f[1]);
-          u.y = Io<T>::pack2(f[2], f[3]);
-          u.z = Io<T>::pack2(f[4], f[5]);
-          u.w = Io<T>::pack2(f[6], f[7]);
-          ov4[q] = u;
         }
       }
+      gi += my_nb;
     }
   }
 
@@ -558,6 +652,7 @@ cudaError_t run_tc(const AttnArgs& a, cudaStream_t s) {
   p.os_b = a.os[0];
   p.os_h = a.os[1];
   p.os_s = a.os[2];
+  p.B = static_cast<int>(a.B);
   p.H = static_cast<int>(a.H);
   p.Sq = static_cast<int>(a.Sq);
   p.Skv = static_cast<int>(a.Skv);
@@ -566,7 +661,11 @@ cudaError_t run_tc(const AttnArgs& a, cudaStream_t s) {
   p.causal = a.causal;
   unsigned int* err = device_error_word();
   if (err == nullptr) return cudaErrorInvalidDevice;
-  const dim3 grid(static_cast<unsigned>(p.n_qtiles), static_cast<unsigned>(a.H), static_cast<unsigned>(a.B));
+  // Persistent: one CTA per SM (the 512-column TMEM allocation allows one),
+  // each looping over work items; never more CTAs than items.
+  const int64_t n_items = static_cast<int64_t>(p.n_qtiles) * a.H * a.B;
+  const int sms = device_num_sms();
+  const dim3 grid(static_cast<unsigned>(n_items < sms ? n_items : sms));
   return launch_pdl(kern, grid, dim3(kAttnThreads), static_cast<size_t>(kAttnSmem), s, mq, mk, mv, p, err);
 }
 
