@@ -7,9 +7,10 @@
   bias_gelu         16384 x 3072 fp16 + bias, tanh GELU   (201.33 MB moved)
   stack             12-layer encoder stack, batch 64 split over the ranks
 
-Each step replays a CUDA graph of 10 back-to-back launches (the stack: one
-forward) between CUDA events, with a 256 MB L2-flush write between steps
-outside the events; the per-launch time is the step time / 10. Used by bench.py.
+Each step replays a CUDA graph of 10 back-to-back launches between CUDA
+events, with a 256 MB L2-flush write between steps outside the events; the
+launches cycle over enough distinct buffer sets that none finds its inputs
+in L2; the per-launch time is the step time / 10. Used by bench.py.
 """
 from __future__ import annotations
 
@@ -30,16 +31,19 @@ def _peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def _time_steps(fn, steps, warmup, flush, reps=10):
-    """Per-launch device time of ``fn`` (ms), one value per step.
+def _time_steps(fns, steps, warmup, flush):
+    """Per-launch device time (ms), one value per step.
 
-    ``fn`` is captured REPS times into one CUDA graph; a step replays the
-    graph between CUDA events, after a 256 MB L2-flush write outside them, and
-    counts time / REPS, so host launch cost is not in the number (the first
-    launch of a step reads cold L2, the others warm).
+    ``fns`` are launches on distinct buffer sets, enough of them that their
+    working sets together exceed L2 (no launch finds its inputs left in L2 by
+    the previous one). They are captured back to back, REPS = 10 launches
+    cycling over the sets, into one CUDA graph; a step replays the graph
+    between CUDA events after a 256 MB L2-flush write outside them and counts
+    time / REPS, so host launch cost is not in the number.
     """
     from lunara_b200.runtime.encoder import GraphRunner
-    runner = GraphRunner(lambda: [fn() for _ in range(reps)])
+    reps = 10
+    runner = GraphRunner(lambda: [fns[i % len(fns)]() for i in range(reps)])
     stream = torch.cuda.current_stream()
     for _ in range(warmup):
         flush.zero_()
@@ -58,6 +62,11 @@ def _time_steps(fn, steps, warmup, flush, reps=10):
     return times
 
 
+def _rotations(working_set_bytes: int) -> int:
+    """Buffer sets needed so that consecutive launches never share data in L2."""
+    return max(1, min(10, -(-(256 << 20) // working_set_bytes)))
+
+
 def run(workload, args, rank, world, device):
     from oracle import inputs
     from lunara_b200.runtime import ops
@@ -67,10 +76,11 @@ def run(workload, args, rank, world, device):
     if workload == "gemm":
         a, b, bias = inputs.gemm_inputs()
         a, b, bias = a.half().to(device), b.half().to(device), bias.half().to(device)
-        c = torch.empty(4096, 4096, dtype=torch.float16, device=device)
-        t_plain = _time_steps(lambda: ops.gemm(a, b, c), args.steps, args.warmup, flush)
-        t_fused = _time_steps(lambda: ops.gemm(a, b, c, bias=bias, activation="gelu_tanh"), args.steps,
-                              args.warmup, flush)
+        n = _rotations(3 * 4096 * 4096 * 2)
+        sets = [(a.clone(), b.clone(), torch.empty(4096, 4096, dtype=torch.float16, device=device)) for _ in range(n)]
+        t_plain = _time_steps([lambda s=s_: ops.gemm(s[0], s[1], s[2]) for s_ in sets], args.steps, args.warmup, flush)
+        t_fused = _time_steps([lambda s=s_: ops.gemm(s[0], s[1], s[2], bias=bias, activation="gelu_tanh")
+                               for s_ in sets], args.steps, args.warmup, flush)
         flops = 2.0 * 4096 ** 3
         tp = flops / (statistics.median(t_plain) * 1e-3) / 1e12
         tf = flops / (statistics.median(t_fused) * 1e-3) / 1e12
@@ -82,8 +92,10 @@ def run(workload, args, rank, world, device):
     elif workload in ("attention", "attention_causal"):
         causal = workload == "attention_causal"
         q, k, v = (t.half().to(device) for t in inputs.attention_inputs())
-        o = torch.empty_like(q)
-        t = _time_steps(lambda: ops.attention(q, k, v, causal=causal, out=o), args.steps, args.warmup, flush)
+        n = _rotations(4 * q.numel() * 2)
+        sets = [(q.clone(), k.clone(), v.clone(), torch.empty_like(q)) for _ in range(n)]
+        t = _time_steps([lambda s=s_: ops.attention(s[0], s[1], s[2], causal=causal, out=s[3]) for s_ in sets],
+                        args.steps, args.warmup, flush)
         flops = 4.0 * 2 * 12 * 2048 * 2048 * 64 * (0.5 if causal else 1.0)
         ach = flops / (statistics.median(t) * 1e-3) / 1e12
         line.update(metric=f"attention B2 H12 S2048 D64 fp16 {'causal' if causal else 'non-causal'} TFLOP/s",
@@ -95,8 +107,10 @@ def run(workload, args, rank, world, device):
     elif workload == "layernorm":
         x, w, b = inputs.layernorm_inputs()
         x, w, b = x.half().to(device), w.half().to(device), b.half().to(device)
-        y = torch.empty_like(x)
-        t = _time_steps(lambda: ops.layernorm(x, w, b, 1e-5, out=y), args.steps, args.warmup, flush)
+        n = _rotations(2 * x.numel() * 2)
+        sets = [(x.clone(), torch.empty_like(x)) for _ in range(n)]
+        t = _time_steps([lambda s=s_: ops.layernorm(s[0], w, b, 1e-5, out=s[1]) for s_ in sets],
+                        args.steps, args.warmup, flush)
         nbytes = 2.0 * 16384 * 768 * 2 + 2 * 768 * 2
         gbs = nbytes / (statistics.median(t) * 1e-3) / 1e9
         line.update(metric="LayerNorm 16384x768 fp16 GB/s", value=gbs, unit="GB/s", dtype="f16",
@@ -106,8 +120,10 @@ def run(workload, args, rank, world, device):
     elif workload == "bias_gelu":
         x, bias = inputs.bias_gelu_inputs()
         x, bias = x.half().to(device), bias.half().to(device)
-        y = torch.empty_like(x)
-        t = _time_steps(lambda: ops.bias_act(x, bias, "gelu_tanh", out=y), args.steps, args.warmup, flush)
+        n = _rotations(2 * x.numel() * 2)
+        sets = [(x.clone(), torch.empty_like(x)) for _ in range(n)]
+        t = _time_steps([lambda s=s_: ops.bias_act(s[0], bias, "gelu_tanh", out=s[1]) for s_ in sets],
+                        args.steps, args.warmup, flush)
         nbytes = 2.0 * 16384 * 3072 * 2 + 3072 * 2
         gbs = nbytes / (statistics.median(t) * 1e-3) / 1e9
         line.update(metric="bias+GELU 16384x3072 fp16 GB/s", value=gbs, unit="GB/s", dtype="f16",
@@ -121,7 +137,7 @@ def run(workload, args, rank, world, device):
         xs = x[rank * per_rank:(rank + 1) * per_rank]
         st = EncoderStack(ws, batch=per_rank, seq=512, num_heads=12, device=device)
         st.x.copy_(xs.half().reshape(-1, 768).to(device))
-        t = _time_steps(st.run_kernels, args.steps, args.warmup, flush, reps=1)
+        t = _time_steps([st.run_kernels], args.steps, args.warmup, flush)
         total = sum(t)
         if world > 1:
             import torch.distributed as dist
