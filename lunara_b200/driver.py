@@ -152,6 +152,7 @@ class Compiler:
         print(f"[lunara] Compiling {model_path.name} → {out}/")
         mlir_path = out / "lowered.mlir"
         self._run_lunara_opt(model_path, mlir_path)
+        self._model_path = model_path
         specs = self._extract_kernel_specs(mlir_path, name)
         emitter = KernelEmitter(str(out / "kernels"))
         for spec in specs:
@@ -180,7 +181,24 @@ class Compiler:
             print(f"[warn] lunara-opt failed:\n{e.stderr}")
 
     def _extract_kernel_specs(self, mlir_path: Path, model_name: str) -> List[KernelSpec]:
-        """The canonical encoder-block kernel set (the reference's behaviour, driver.py:208-216)."""
+        """Kernel specs of the model being compiled.
+
+        The reference returns the canonical encoder-block kernel set here
+        whatever the model (driver.py:208-216). This reads the ONNX graph
+        itself (lunara_b200.frontend.onnx_graph) and derives the kernel list
+        from it; a file that is not a readable ONNX model, or a graph with no
+        kernel-producing node, falls back to the canonical block set.
+        """
+        from lunara_b200.frontend.onnx_graph import OnnxFormatError, graph_kernel_specs, load_onnx
+        model_path = getattr(self, "_model_path", None)
+        if model_path is not None:
+            try:
+                specs = graph_kernel_specs(load_onnx(model_path), self.dtype)
+            except (OSError, OnnxFormatError) as e:
+                print(f"[warn] {model_path}: not a readable ONNX model ({e}); using the encoder-block kernels")
+                specs = []
+            if specs:
+                return specs
         return _default_transformer_specs(model_name, self.dtype)
 
     def _autotune(self, specs: List[KernelSpec]) -> Dict[str, TuningResult]:
