@@ -227,7 +227,8 @@ def bench_block(args, rank, world, device):
     fns = blk.kernel_fns()
     kernel_runners = {name: GraphRunner(lambda f=f: [f() for _ in range(reps)]) for name, f in fns.items()}
 
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    # 256 MB (twice the 126 MB L2), int64 so that the fill kernel stores wide words.
+    flush = torch.empty(32 * 1024 * 1024, dtype=torch.int64, device=device)
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
         flush.zero_()

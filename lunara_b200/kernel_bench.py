@@ -71,7 +71,7 @@ def run(workload, args, rank, world, device):
     from oracle import inputs
     from lunara_b200.runtime import ops
     hbm, tflops_peak, src = _peaks()
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    flush = torch.empty(32 << 20, dtype=torch.int64, device=device)   # 256 MB, wide stores
     line = {"steps": args.steps, "warmup": args.warmup, "n_gpus": world, "data": "synthetic (seeded)"}
     if workload == "gemm":
         a, b, bias = inputs.gemm_inputs()
