@@ -49,6 +49,22 @@ def test_attention_cross_lengths(Sq, Skv):
     check_close(o, oracle.attention(q, k, v), torch.float16, f"attention {Sq}x{Skv}")
 
 
+@pytest.mark.parametrize("Sq,Skv", [(300, 129), (129, 300), (257, 640)])
+def test_attention_cross_lengths_causal(Sq, Skv):
+    """Causal mask on absolute positions (key <= query) with different query / key lengths."""
+    q, k, v = _qkv(2, 3, Sq, Skv, 64, torch.float16, 7 * Sq + Skv)
+    o = _ops().attention(q.cuda(), k.cuda(), v.cuda(), causal=True)
+    check_close(o, oracle.attention(q, k, v, True), torch.float16, f"causal attention {Sq}x{Skv}")
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_many_items_bf16(causal):
+    """More 128-row work items than SMs (ragged last tile): persistent CTAs take several items."""
+    q, k, v = _qkv(3, 8, 1000, 1000, 64, torch.bfloat16, 5)
+    o = _ops().attention(q.cuda(), k.cuda(), v.cuda(), causal=causal)
+    check_close(o, oracle.attention(q, k, v, causal), torch.bfloat16, f"bf16 attention B3H8S1000 causal={causal}")
+
+
 def test_attention_fused_qkv_layout():
     ops = _ops()
     B, S, H, D = 2, 384, 4, 64
