@@ -36,12 +36,20 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kEpiWarps = 8;        // two warps per TMEM lane quarter, each owning half the tile's columns
+// Epilogue: three warps per TMEM lane quarter (a warp may only read the 32
+// lanes of its quarter, warp % 4); the tile's 32-column chunks are dealt to the
+// three column slices round-robin. 14 warps in all keep 128 registers per
+// thread (at most 4 warps share an SM sub-partition's 64 KB register file).
+constexpr int kEpiWarps = 12;
+constexpr int kEpiSlices = kEpiWarps / 4;
+constexpr int kMaxWarpChunks = (256 / 32 + kEpiSlices - 1) / kEpiSlices;  // chunks per warp at the widest tile
 constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kGemmThreads = 64 + kEpiThreads;
 constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in limit per block on sm_100
 constexpr int kStageC = 2048;       // per epilogue warp: one 32 x 32 16-bit output chunk
-constexpr int kSmemReserve = 6144 + kEpiWarps * kStageC;  // barriers, bias staging, output staging, alignment
+constexpr int kBiasPerWarp = 32 * kMaxWarpChunks;   // fp32 bias values staged per epilogue warp
+// Alignment slack, barriers and flags, bias staging, output staging.
+constexpr int kSmemReserve = 1024 + 512 + kEpiWarps * kBiasPerWarp * 4 + kEpiWarps * kStageC;
 
 struct EpiParams {
   void* C;
@@ -108,18 +116,6 @@ __device__ __forceinline__ void load_residual(ResChunk& rc, int row, int col0, c
 #pragma unroll
     for (int q = 0; q < 4; ++q) rc.q[q] = __ldg(rv + q);
   }
-}
-
-// Pulls this lane's residual row segment [c0, c0 + count) into L2 while the
-// tile's main loop is still running, so that the epilogue's residual loads
-// (issued only once the accumulator is complete) hit L2 instead of HBM.
-template <typename T>
-__device__ __forceinline__ void prefetch_residual(int row, int c0, int count, const EpiParams& ep) {
-  if (ep.residual == nullptr || row >= ep.M) return;
-  const char* p = reinterpret_cast<const char*>(static_cast<const T*>(ep.residual) +
-                                                static_cast<int64_t>(row) * ep.ldr + c0);
-  const int bytes = min(count, ep.N - c0) * static_cast<int>(sizeof(T));
-  for (int off = 0; off < bytes; off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + off));
 }
 
 // Epilogue for 32 consecutive accumulator columns of one row: + bias (staged
@@ -221,79 +217,78 @@ __device__ __forceinline__ void epilogue_pack(const uint32_t (&acc)[32], int row
   for (int i = 0; i < 16; ++i) pk[i] = Io<T>::pack2(f[2 * i], f[2 * i + 1]);
 }
 
-// One 32-row x 32-column output chunk of a warp: either staged in the warp's
-// shared buffer with the 64-byte swizzle (16-byte chunk q of row r at slot
-// q ^ ((r >> 1) & 3), conflict-free) and written by one TMA store that clips
-// rows >= M and columns >= N, or stored directly by each thread.
-template <typename T, int EPI>
-__device__ __forceinline__ void epilogue_out(const uint32_t (&acc)[32], int row, int col0, int row0_warp,
-                                             const float* s_bias, const ResChunk& rc, const EpiParams& ep,
-                                             const CUtensorMap* tma_c, uint8_t* s_stage, int lane) {
-  if (ep.tma_store) {
-    uint32_t pk[16];
-    epilogue_pack<T, EPI>(acc, row, col0, s_bias, rc, ep, pk);
-    if (lane == 0) bulk_wait_group_read<0>();   // the previous chunk's store has read the buffer
-    __syncwarp();
-    uint8_t* dst = s_stage + lane * 64;
+// One 32-row x 32-column output chunk of a warp, already rounded and packed:
+// staged in the warp's shared buffer with the 64-byte swizzle (16-byte chunk q
+// of row r at slot q ^ ((r >> 1) & 3), conflict-free) and written by one TMA
+// store that clips rows >= M and columns >= N.
+__device__ __forceinline__ void store_chunk_tma(const uint32_t (&pk)[16], int col0, int row0_warp,
+                                                const CUtensorMap* tma_c, uint8_t* s_stage, int lane) {
+  if (lane == 0) bulk_wait_group_read<0>();   // the previous chunk's store has read the buffer
+  __syncwarp();
+  uint8_t* dst = s_stage + lane * 64;
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
-      *reinterpret_cast<uint4*>(dst + ((q ^ ((lane >> 1) & 3)) << 4)) =
-          make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_2d(tma_c, s_stage, col0, row0_warp);
-      bulk_commit_group();
-    }
-  } else {
-    epilogue_chunk<T, EPI>(acc, row, col0, s_bias, rc, ep);
+  for (int q = 0; q < 4; ++q)
+    *reinterpret_cast<uint4*>(dst + ((q ^ ((lane >> 1) & 3)) << 4)) =
+        make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tma_c, s_stage, col0, row0_warp);
+    bulk_commit_group();
   }
 }
 
-// The epilogue of one accumulator tile for one warp: `kHalf` columns starting at
-// c0 for the 32 rows starting at row0_warp (this lane's row = row0_warp + lane),
-// read from TMEM at t_row one 32-column chunk ahead of their use. res[0] holds
-// the residual of the first chunk, loaded by the caller before the accumulator
-// was ready.
+// The epilogue of one accumulator tile for one warp: its chunks
+// c = slice + j * kEpiSlices of the 32 rows starting at row0_warp (this lane's
+// row = row0_warp + lane). A chunk's TMEM load and residual load are issued as
+// soon as the previous chunk has been packed, so they run under that chunk's
+// store; `res` holds the first chunk's residual, loaded by the caller before
+// the accumulator was ready.
 template <typename T, int BN, int EPI>
-__device__ __forceinline__ void epilogue_tile(uint32_t t_row, int row0_warp, int c0, const float* sb,
+__device__ __forceinline__ void epilogue_tile(uint32_t t_tile, int row0_warp, int n0, int slice, const float* sb,
                                               const EpiParams& ep, const CUtensorMap* tma_c, uint8_t* s_stage,
-                                              int lane, ResChunk (&res)[2]) {
-  constexpr int kHalf = BN / 2;
-  constexpr int kChunks = kHalf / 32;
+                                              int lane, ResChunk& res) {
+  constexpr int kChunks = BN / 32;
+  static_assert(kChunks <= kEpiSlices * kMaxWarpChunks, "epilogue chunk split");
+  if (slice >= kChunks) return;
   const int row = row0_warp + lane;
-  // Chunks are processed in pairs (two register buffers, compile-time
-  // indices); the loop itself is not unrolled to keep the code small.
-  uint32_t v[2][32];
-  tmem_ld_32x32b_x32(t_row, v[0]);
-#pragma unroll 1
-  for (int c = 0; c < kChunks; c += 2) {
-    tmem_ld_wait_regs(v[0]);
-    if (c + 1 < kChunks) {
-      tmem_ld_32x32b_x32(t_row + (c + 1) * 32, v[1]);
-      load_residual<T>(res[1], row, c0 + (c + 1) * 32, ep);
-    }
-    epilogue_out<T, EPI>(v[0], row, c0 + c * 32, row0_warp, sb + c * 32, res[0], ep, tma_c, s_stage, lane);
-    if (c + 1 < kChunks) {
-      tmem_ld_wait_regs(v[1]);
-      if (c + 2 < kChunks) {
-        tmem_ld_32x32b_x32(t_row + (c + 2) * 32, v[0]);
-        load_residual<T>(res[0], row, c0 + (c + 2) * 32, ep);
+  uint32_t v[32];
+  tmem_ld_32x32b_x32(t_tile + slice * 32, v);
+#pragma unroll
+  for (int j = 0; j < kMaxWarpChunks; ++j) {
+    const int c = slice + j * kEpiSlices;
+    if (c >= kChunks) break;
+    const bool more = c + kEpiSlices < kChunks;
+    tmem_ld_wait_regs(v);
+    if (ep.tma_store) {
+      uint32_t pk[16];
+      epilogue_pack<T, EPI>(v, row, n0 + c * 32, sb + j * 32, res, ep, pk);
+      if (more) {
+        tmem_ld_32x32b_x32(t_tile + (c + kEpiSlices) * 32, v);
+        load_residual<T>(res, row, n0 + (c + kEpiSlices) * 32, ep);
       }
-      epilogue_out<T, EPI>(v[1], row, c0 + (c + 1) * 32, row0_warp, sb + (c + 1) * 32, res[1], ep, tma_c,
-                           s_stage, lane);
+      store_chunk_tma(pk, n0 + c * 32, row0_warp, tma_c, s_stage, lane);
+    } else {
+      epilogue_chunk<T, EPI>(v, row, n0 + c * 32, sb + j * 32, res, ep);
+      if (more) {
+        tmem_ld_32x32b_x32(t_tile + (c + kEpiSlices) * 32, v);
+        load_residual<T>(res, row, n0 + (c + kEpiSlices) * 32, ep);
+      }
     }
   }
 }
 
-// Stage this warp's slice of the bias (fp32) in its own shared-memory region;
+// Stage the bias (fp32) of this warp's chunks in its own shared-memory region;
 // only this warp reads it, so __syncwarp orders writes and reads.
-template <typename T>
-__device__ __forceinline__ void stage_bias(float* sb, int c0, int count, const EpiParams& ep, int lane) {
+template <typename T, int BN>
+__device__ __forceinline__ void stage_bias(float* sb, int n0, int slice, const EpiParams& ep, int lane) {
   if (ep.bias == nullptr) return;
-  for (int i = lane; i < count; i += 32) {
-    const int col = c0 + i;
-    sb[i] = col < ep.N ? Io<T>::to_f(static_cast<const T*>(ep.bias)[col]) : 0.f;
+#pragma unroll
+  for (int j = 0; j < kMaxWarpChunks; ++j) {
+    const int c = slice + j * kEpiSlices;
+    if (c >= BN / 32) break;
+    const int col = n0 + c * 32 + lane;
+    sb[j * 32 + lane] = col < ep.N ? Io<T>::to_f(static_cast<const T*>(ep.bias)[col]) : 0.f;
   }
 }
 
@@ -323,7 +318,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* drain_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* s_bias = reinterpret_cast<float*>(drain_bar + 2);  // [8 epilogue warps][128] fp32
+  float* s_bias = reinterpret_cast<float*>(drain_bar + 2);  // [kEpiWarps][kBiasPerWarp] fp32
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -455,29 +450,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ----------------------------------------------------------- epilogue --
-    // Warps 2..9: warp & 3 is the TMEM lane quarter it may read (rows
-    // 32*q .. 32*q+31 of the tile); warps 2-5 take the first half of the
-    // tile's columns, warps 6-9 the second half.
-    constexpr int kHalf = BN / 2;
+    // Warps 2..13: warp & 3 is the TMEM lane quarter it may read (rows
+    // 32*q .. 32*q+31 of the tile); (warp - 2) / 4 is its column slice.
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
-    float* sb = s_bias + (warp - 2) * 128;
+    const int slice = (warp - 2) >> 2;
+    float* sb = s_bias + (warp - 2) * kBiasPerWarp;
     uint8_t* s_stage = sC + (warp - 2) * kStageC;
     uint32_t acc = 0, acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int m0 = (tile % m_tiles) * BM;
       const int n0 = (tile / m_tiles) * BN;
-      const int c0 = n0 + half * kHalf;
-      ResChunk res[2];
-      prefetch_residual<T>(m0 + quarter * 32 + lane, c0, kHalf, ep);
-      load_residual<T>(res[0], m0 + quarter * 32 + lane, c0, ep);
-      stage_bias<T>(sb, c0, kHalf, ep, lane);
+      ResChunk res;
+      if (slice < BN / 32) load_residual<T>(res, m0 + quarter * 32 + lane, n0 + slice * 32, ep);
+      stage_bias<T, BN>(sb, n0, slice, ep, lane);
       __syncwarp();
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, err, kErrGemmEpilogue)) break;
       tc_fence_after();
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * ACC_STRIDE +
-                             half * kHalf;
-      epilogue_tile<T, BN, EPI>(t_row, m0 + quarter * 32, c0, sb, ep, &tma_c, s_stage, lane, res);
+      const uint32_t t_tile = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * ACC_STRIDE;
+      epilogue_tile<T, BN, EPI>(t_tile, m0 + quarter * 32, n0, slice, sb, ep, &tma_c, s_stage, lane, res);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
@@ -687,27 +677,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ----------------------------------------------------------- epilogue --
-    constexpr int kHalf = BN / 2;
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int slice = (warp - 2) >> 2;
     const uint32_t leader_tempty = smem_u32(tempty_bar) & kPeerBitMask;
-    float* sb = s_bias + (warp - 2) * 128;
+    float* sb = s_bias + (warp - 2) * kBiasPerWarp;
     uint8_t* s_stage = sC + (warp - 2) * kStageC;
     uint32_t acc = 0, acc_phase = 0;
     for (int tile = cluster_id; tile < num_tiles; tile += num_clusters) {
       const int m0 = (tile % m_tiles) * 2 * BM + static_cast<int>(rank) * BM;
       const int n0 = (tile / m_tiles) * BN;
-      const int c0 = n0 + half * kHalf;
-      ResChunk res[2];
-      prefetch_residual<T>(m0 + quarter * 32 + lane, c0, kHalf, ep);
-      load_residual<T>(res[0], m0 + quarter * 32 + lane, c0, ep);
-      stage_bias<T>(sb, c0, kHalf, ep, lane);
+      ResChunk res;
+      if (slice < BN / 32) load_residual<T>(res, m0 + quarter * 32 + lane, n0 + slice * 32, ep);
+      stage_bias<T, BN>(sb, n0, slice, ep, lane);
       __syncwarp();
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, err, kErrGemmEpilogue)) break;
       tc_fence_after();
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * ACC_STRIDE +
-                             half * kHalf;
-      epilogue_tile<T, BN, EPI>(t_row, m0 + quarter * 32, c0, sb, ep, &tma_c, s_stage, lane, res);
+      const uint32_t t_tile = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * ACC_STRIDE;
+      epilogue_tile<T, BN, EPI>(t_tile, m0 + quarter * 32, n0, slice, sb, ep, &tma_c, s_stage, lane, res);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_tempty + acc * 8);
