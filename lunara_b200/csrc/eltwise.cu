@@ -220,10 +220,13 @@ __global__ void __launch_bounds__(kThreads) bias_act_scalar_kernel(const T* __re
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Grid of whole waves: `waves` CTAs of 256 threads per SM, capped by the work.
+// Grid for the grid-stride loops: enough CTAs of 256 threads for `per_thread`
+// items each, capped at 64 CTAs per SM (8 waves). On B200 more, shorter-lived
+// CTAs streamed faster than one resident wave looping over the data (bias +
+// GELU, 16384 x 3072 fp16: 8 CTAs per SM 5.5 TB/s, 16: 5.8, 32: 6.1, 64: 6.3).
 unsigned grid_for(int64_t work_items, int per_thread) {
   const int64_t need = ceil_div64(work_items, int64_t{kThreads} * per_thread);
-  const int64_t cap = int64_t{device_num_sms()} * 8;
+  const int64_t cap = int64_t{device_num_sms()} * 64;
   int64_t g = need < cap ? need : cap;
   return static_cast<unsigned>(g < 1 ? 1 : g);
 }
