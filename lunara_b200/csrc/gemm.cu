@@ -814,8 +814,12 @@ bool encode_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, ui
 // cycles of one 64-deep K block are bounded by the tensor pipe (2*BN for both
 // the 128-row and the 256-row pair MMA) and by the operand bytes each CTA must
 // pull from L2 (about 60 B/cycle/SM sustained when every SM streams); tiles
-// are handed out in rounds over the persistent CTAs (pairs), plus a fixed
-// per-tile overhead for fill, drain and the epilogue hand-off.
+// are handed out in rounds over the persistent CTAs (pairs). A CTA pair pays a
+// further ~3200 cycles per tile (cross-CTA barriers, cluster synchronisation,
+// the pair's epilogue hand-off): fitted to a sweep of 12 shapes on B200
+// (block, 12-layer-stack and square GEMMs), where it picks the fastest plan or
+// one within 4% for every shape (single-CTA 128x192 tiles for N=768 at K=768,
+// CTA pairs for long K loops and wide N).
 struct GemmPlan {
   int block_n;
   bool pair;
@@ -829,7 +833,7 @@ double gemm_cost(int64_t M, int64_t N, int64_t K, GemmPlan p, int sms) {
   const int64_t rounds = ceil_div64(tiles, units);
   const double bytes = BM * BK * 2.0 + (p.pair ? p.block_n / 2 : p.block_n) * BK * 2.0;
   const double per_kb = std::max(2.0 * p.block_n, bytes / kL2BytesPerCycle);
-  return static_cast<double>(rounds) * (static_cast<double>(ceil_div64(K, BK)) * per_kb + 800.0);
+  return static_cast<double>(rounds) * (static_cast<double>(ceil_div64(K, BK)) * per_kb + (p.pair ? 3200.0 : 0.0));
 }
 
 GemmPlan choose_plan(int64_t M, int64_t N, int64_t K, int sms, int block_n, int cta_pair, bool b_kmajor) {
