@@ -817,22 +817,26 @@ bool encode_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, ui
 // are handed out in rounds over the persistent CTAs (pairs). A CTA pair pays a
 // further ~3200 cycles per tile (cross-CTA barriers, cluster synchronisation,
 // the pair's epilogue hand-off): fitted to a sweep of 12 shapes on B200
-// (block, 12-layer-stack and square GEMMs), where it picks the fastest plan or
-// one within 4% for every shape (single-CTA 128x192 tiles for N=768 at K=768,
-// CTA pairs for long K loops and wide N).
+// (block, 12-layer-stack and square GEMMs), where, with the one-round rate
+// below, it picks the fastest plan or one within 2% for every shape
+// (single-CTA 128x192 tiles for N=768 outputs of 4096 rows, CTA pairs for
+// wide N and for many rounds).
 struct GemmPlan {
   int block_n;
   bool pair;
 };
 
 double gemm_cost(int64_t M, int64_t N, int64_t K, GemmPlan p, int sms) {
-  constexpr double kL2BytesPerCycle = 60.0;
   const int tile_m = p.pair ? 2 * BM : BM;
   const int64_t tiles = ceil_div64(M, tile_m) * ceil_div64(N, p.block_n);
   const int64_t units = p.pair ? sms / 2 : sms;
   const int64_t rounds = ceil_div64(tiles, units);
+  // Single-CTA tiles that all fit in one round stream their operands at a
+  // higher rate than the all-SMs-busy figure (measured: 4096x768 at K=768 and
+  // K=3072, 2048^3), so they are costed at 80 B/cycle instead of 60.
+  const double l2_bytes_per_cycle = (!p.pair && rounds == 1) ? 80.0 : 60.0;
   const double bytes = BM * BK * 2.0 + (p.pair ? p.block_n / 2 : p.block_n) * BK * 2.0;
-  const double per_kb = std::max(2.0 * p.block_n, bytes / kL2BytesPerCycle);
+  const double per_kb = std::max(2.0 * p.block_n, bytes / l2_bytes_per_cycle);
   return static_cast<double>(rounds) * (static_cast<double>(ceil_div64(K, BK)) * per_kb + (p.pair ? 3200.0 : 0.0));
 }
 
