@@ -324,6 +324,12 @@ int lunara_qkv_split(const void* qkv, void* q, void* k, void* v, int64_t B, int6
   if (B < 0 || S < 0 || H < 0 || D < 0) return fail(LUNARA_ERR_INVALID_ARG, "lunara_qkv_split: negative shape");
   if (B == 0 || S == 0 || H == 0 || D == 0) return ok();
   if (!qkv || !q || !k || !v) return fail(LUNARA_ERR_INVALID_ARG, "lunara_qkv_split: NULL pointer");
+  if (elem_bytes != 1 && elem_bytes != 2 && elem_bytes != 4 && elem_bytes != 8)
+    return fail(LUNARA_ERR_INVALID_ARG, "lunara_qkv_split: elem_bytes %lld", (long long)elem_bytes);
+  bool handled = false;
+  const cudaError_t e = launch_qkv_split(qkv, q, k, v, B, S, H, D, elem_bytes, static_cast<cudaStream_t>(stream),
+                                         &handled);
+  if (handled) return from_cuda(e, "lunara_qkv_split");
   // Source viewed as [B, S, 3, H, D]; destination [B, H, S, D] for each of q, k, v.
   const int64_t sizes[4] = {B, H, S, D};
   const int64_t strides[4] = {S * 3 * H * D, D, 3 * H * D, 1};

@@ -62,6 +62,42 @@ __global__ void __launch_bounds__(kThreads) copy_strided_kernel(const U* __restr
 
 bool al(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// QKV split + head reshape in one launch: source [B, S, 3, H, DU] in 16-byte
+// units, destinations [B, H, S, DU] for q, k and v. grid = (ceil(S*DU /
+// (kQkvUnits*256)), B*H, 3): each thread moves kQkvUnits units 256 apart
+// (both loads before either store); a warp reads 128-byte head rows of
+// consecutive positions and writes 512 contiguous bytes. The only division
+// per unit is by DU (position and unit within the head row).
+constexpr int kQkvUnits = 4;
+
+__global__ void __launch_bounds__(kThreads) qkv_split_kernel(const uint4* __restrict__ src, uint4* __restrict__ q,
+                                                             uint4* __restrict__ k, uint4* __restrict__ v,
+                                                             int S, int H, int DU) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int bh = static_cast<int>(blockIdx.y);
+  const int b = bh / H;
+  const int h = bh - b * H;
+  const int which = static_cast<int>(blockIdx.z);
+  uint4* dst = which == 0 ? q : (which == 1 ? k : v);
+  const int t0 = static_cast<int>(blockIdx.x) * (kQkvUnits * kThreads) + static_cast<int>(threadIdx.x);
+  uint4 val[kQkvUnits];
+#pragma unroll
+  for (int j = 0; j < kQkvUnits; ++j) {
+    const int t = t0 + j * kThreads;
+    if (t < S * DU) {
+      const int s = t / DU;
+      const int u = t - s * DU;
+      val[j] = src[((static_cast<int64_t>(b) * S + s) * 3 + which) * H * DU + static_cast<int64_t>(h) * DU + u];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kQkvUnits; ++j) {
+    const int t = t0 + j * kThreads;
+    if (t < S * DU) dst[static_cast<int64_t>(bh) * S * DU + t] = val[j];
+  }
+}
+
 template <typename U>
 cudaError_t gather_u(const void* src, const int64_t* index, void* dst, int64_t n_index, int64_t src_rows,
                      int64_t units, cudaStream_t s) {
@@ -92,6 +128,20 @@ cudaError_t launch_gather(const void* src, const int64_t* index, void* dst, int6
   if (row_bytes % 4 == 0 && al(src, 4) && al(dst, 4))
     return gather_u<uint32_t>(src, index, dst, n_index, src_rows, row_bytes / 4, stream);
   return gather_u<uint8_t>(src, index, dst, n_index, src_rows, row_bytes, stream);
+}
+
+cudaError_t launch_qkv_split(const void* qkv, void* q, void* k, void* v, int64_t B, int64_t S, int64_t H,
+                             int64_t D, int64_t elem_bytes, cudaStream_t stream, bool* handled) {
+  *handled = false;
+  const int64_t row_bytes = D * elem_bytes;
+  if (row_bytes % 16 != 0 || !al(qkv, 16) || !al(q, 16) || !al(k, 16) || !al(v, 16)) return cudaSuccess;
+  const int64_t du = row_bytes / 16;
+  if (B * H > 65535 || S * du >= (int64_t{1} << 31) || H * du >= (int64_t{1} << 31)) return cudaSuccess;
+  *handled = true;
+  const dim3 grid(static_cast<unsigned>(ceil_div64(S * du, kQkvUnits * kThreads)), static_cast<unsigned>(B * H), 3);
+  return launch_pdl(qkv_split_kernel, grid, dim3(kThreads), 0, stream, static_cast<const uint4*>(qkv),
+                    static_cast<uint4*>(q), static_cast<uint4*>(k), static_cast<uint4*>(v), static_cast<int>(S),
+                    static_cast<int>(H), static_cast<int>(du));
 }
 
 cudaError_t launch_copy_strided(const void* src, void* dst, int ndim, const int64_t* sizes,

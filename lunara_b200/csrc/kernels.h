@@ -48,6 +48,11 @@ cudaError_t launch_bias_act(const void* X, const void* bias, void* Y, int64_t ro
 
 cudaError_t launch_gather(const void* src, const int64_t* index, void* dst, int64_t n_index, int64_t src_rows,
                           int64_t row_bytes, cudaStream_t stream);
+// Single-launch QKV split for 16-byte-aligned head rows; sets *handled to
+// false (and launches nothing) when the shape or alignment needs the general
+// strided copy instead.
+cudaError_t launch_qkv_split(const void* qkv, void* q, void* k, void* v, int64_t B, int64_t S, int64_t H,
+                             int64_t D, int64_t elem_bytes, cudaStream_t stream, bool* handled);
 cudaError_t launch_copy_strided(const void* src, void* dst, int ndim, const int64_t* sizes,
                                 const int64_t* src_strides, int64_t elem_bytes, cudaStream_t stream);
 

@@ -74,17 +74,17 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// CTA size of the softmax warp-per-row path (8 rows per CTA) and of the
-// one-CTA-per-row fallbacks.
+// CTA size of the one-CTA-per-row fallbacks.
 constexpr int kRowThreads = 256;
-// LayerNorm's warp-per-row path uses 4 rows per CTA: on B200 the smaller CTAs
-// measured 2-15% faster than 8-row CTAs (16384 x 768 fp16: 10.44 vs 10.65 us,
-// 16384 x 1024 bf16: 13.5 vs 15.6 us; 16-row CTAs were slower still).
-constexpr int kLnWarpThreads = 128;
+// The warp-per-row paths use 4 rows per 128-thread CTA: on B200 these measured
+// faster than 8-row CTAs (LayerNorm 16384 x 768 fp16: 10.44 vs 10.65 us, 16384
+// x 1024 bf16: 13.5 vs 15.6 us; softmax 8192 x 4096 fp16: 49.2 vs 62.9 us,
+// 16384 x 1024: 15.8 vs 16.4 us) and 16-row CTAs were slower still.
+constexpr int kWarpRowThreads = 128;
 
 // ------------------------------------------------------------ LayerNorm ----
 template <typename T, int VPL>
-__global__ void __launch_bounds__(kLnWarpThreads) layernorm_warp_kernel(const T* __restrict__ X,
+__global__ void __launch_bounds__(kWarpRowThreads) layernorm_warp_kernel(const T* __restrict__ X,
                                                                      const T* __restrict__ gamma,
                                                                      const T* __restrict__ beta, T* __restrict__ Y,
                                                                      int64_t M, int N, float eps) {
@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(kLnWarpThreads) layernorm_warp_kernel(const T*
   constexpr int EPV = VecTraits<T>::kElems;
   const int nv = N / EPV;
   const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kLnWarpThreads / 32) + (threadIdx.x >> 5);
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kWarpRowThreads / 32) + (threadIdx.x >> 5);
   if (row >= M) return;
   const uint4* xr = reinterpret_cast<const uint4*>(X + row * N);
   float v[VPL][EPV];
@@ -191,14 +191,14 @@ __global__ void __launch_bounds__(kRowThreads) layernorm_block_kernel(const T* _
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <typename T, int VPL>
-__global__ void __launch_bounds__(kRowThreads) softmax_warp_kernel(const T* __restrict__ X, T* __restrict__ Y,
+__global__ void __launch_bounds__(kWarpRowThreads) softmax_warp_kernel(const T* __restrict__ X, T* __restrict__ Y,
                                                                    int64_t M, int N) {
   pdl_wait();
   pdl_launch_dependents();
   constexpr int EPV = VecTraits<T>::kElems;
   const int nv = N / EPV;
   const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kRowThreads / 32) + (threadIdx.x >> 5);
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kWarpRowThreads / 32) + (threadIdx.x >> 5);
   if (row >= M) return;
   const uint4* xr = reinterpret_cast<const uint4*>(X + row * N);
   float v[VPL][EPV];
@@ -279,13 +279,13 @@ cudaError_t layernorm_t(const void* X, const void* g, const void* b, void* Y, in
                       N <= (int64_t{1} << 30);
   const int vpl = vec_ok ? pick_vpl(ceil_div64(N / EPV, 32)) : 0;
   if (vpl > 0) {
-    const dim3 grid(static_cast<unsigned>(ceil_div64(M, kLnWarpThreads / 32)));
+    const dim3 grid(static_cast<unsigned>(ceil_div64(M, kWarpRowThreads / 32)));
     const int n = static_cast<int>(N);
     cudaError_t e = cudaSuccess;
     switch (vpl) {
 #define LN_CASE(V)                                                                               \
   case V:                                                                                        \
-    e = launch_pdl(layernorm_warp_kernel<T, V>, grid, dim3(kLnWarpThreads), 0, s, x, gg, bb, y, M, n, eps); \
+    e = launch_pdl(layernorm_warp_kernel<T, V>, grid, dim3(kWarpRowThreads), 0, s, x, gg, bb, y, M, n, eps); \
     break;
       LN_CASE(1) LN_CASE(2) LN_CASE(3) LN_CASE(4) LN_CASE(6) LN_CASE(8) LN_CASE(12) LN_CASE(16)
 #undef LN_CASE
@@ -305,13 +305,13 @@ cudaError_t softmax_t(const void* X, void* Y, int64_t M, int64_t N, cudaStream_t
   const bool vec_ok = (N % EPV == 0) && aligned16(X) && aligned16(Y) && N <= (int64_t{1} << 30);
   const int vpl = vec_ok ? pick_vpl(ceil_div64(N / EPV, 32)) : 0;
   if (vpl > 0) {
-    const dim3 grid(static_cast<unsigned>(ceil_div64(M, kRowThreads / 32)));
+    const dim3 grid(static_cast<unsigned>(ceil_div64(M, kWarpRowThreads / 32)));
     const int n = static_cast<int>(N);
     cudaError_t e = cudaSuccess;
     switch (vpl) {
 #define SM_CASE(V)                                                                 \
   case V:                                                                          \
-    e = launch_pdl(softmax_warp_kernel<T, V>, grid, dim3(kRowThreads), 0, s, x, y, M, n); \
+    e = launch_pdl(softmax_warp_kernel<T, V>, grid, dim3(kWarpRowThreads), 0, s, x, y, M, n); \
     break;
       SM_CASE(1) SM_CASE(2) SM_CASE(3) SM_CASE(4) SM_CASE(6) SM_CASE(8) SM_CASE(12) SM_CASE(16)
 #undef SM_CASE

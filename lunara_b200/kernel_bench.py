@@ -5,6 +5,10 @@
   attention_causal  same, causal                          (12.88 GFLOP, half)
   layernorm         16384 x 768 fp16                      (50.33 MB moved)
   bias_gelu         16384 x 3072 fp16 + bias, tanh GELU   (201.33 MB moved)
+  softmax           49152 x 512 fp16 row softmax, the block's score shape
+                    (B8 H12 S512 rows of 512 keys; 100.66 MB moved)
+  qkv_split         [8, 512, 2304] fp16 fused projection -> 3 x [8, 12, 512, 64]
+                    (the QKV split + head reshape graph op, bit-exact; 37.75 MB moved)
   stack             12-layer encoder stack, batch 64 split over the ranks
 
 Each step replays a CUDA graph of 10 back-to-back launches between CUDA
@@ -128,6 +132,39 @@ def run(workload, args, rank, world, device):
         gbs = nbytes / (statistics.median(t) * 1e-3) / 1e9
         line.update(metric="bias+GELU 16384x3072 fp16 GB/s", value=gbs, unit="GB/s", dtype="f16",
                     ms_per_step=statistics.median(t), config={"workload": "bias + tanh-GELU 16384x3072 fp16"},
+                    roofline={"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                              "peak_source": f"{src} copy"})
+    elif workload == "softmax":
+        g = torch.Generator().manual_seed(5)
+        x = (2.0 * torch.randn(49152, 512, generator=g)).half().to(device)
+        n = _rotations(2 * x.numel() * 2)
+        sets = [(x.clone(), torch.empty_like(x)) for _ in range(n)]
+        t = _time_steps([lambda s=s_: ops.softmax(s[0], out=s[1]) for s_ in sets], args.steps, args.warmup, flush)
+        nbytes = 2.0 * 49152 * 512 * 2
+        gbs = nbytes / (statistics.median(t) * 1e-3) / 1e9
+        line.update(metric="softmax 49152x512 fp16 GB/s", value=gbs, unit="GB/s", dtype="f16",
+                    ms_per_step=statistics.median(t),
+                    config={"workload": "row softmax 49152x512 fp16 (B8 H12 S512 attention scores)"},
+                    roofline={"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                              "peak_source": f"{src} copy"})
+    elif workload == "qkv_split":
+        from lunara_b200.runtime import _lib
+        lib = _lib.load()
+        g = torch.Generator().manual_seed(6)
+        B, S, H, D = 8, 512, 12, 64
+        qkv = torch.randn(B, S, 3 * H * D, generator=g).half().to(device)
+        n = _rotations(2 * qkv.numel() * 2)
+        sets = [(qkv.clone(), *(torch.empty(B, H, S, D, dtype=torch.half, device=device) for _ in range(3)))
+                for _ in range(n)]
+        def split(s):
+            _lib.check(lib.lunara_qkv_split(s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), s[3].data_ptr(),
+                                            B, S, H, D, 2, torch.cuda.current_stream().cuda_stream))
+        t = _time_steps([lambda s=s_: split(s) for s_ in sets], args.steps, args.warmup, flush)
+        nbytes = 2.0 * qkv.numel() * 2
+        gbs = nbytes / (statistics.median(t) * 1e-3) / 1e9
+        line.update(metric="QKV split [8,512,2304] -> 3x[8,12,512,64] fp16 GB/s", value=gbs, unit="GB/s", dtype="f16",
+                    ms_per_step=statistics.median(t),
+                    config={"workload": "QKV split + head reshape, B8 S512 H12 D64 fp16 (bit-exact copy)"},
                     roofline={"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                               "peak_source": f"{src} copy"})
     elif workload == "stack":

@@ -164,6 +164,19 @@ def test_qkv_split_and_reshape_bit_exact():
     assert torch.equal(r.cpu(), rq.transpose(1, 2).reshape(B, S, H * D))
 
 
+@pytest.mark.parametrize("B,S,H,D,dtype", [(8, 512, 12, 64, torch.float16), (3, 5, 2, 8, torch.bfloat16),
+                                           (2, 33, 4, 60, torch.float16), (1, 7, 3, 12, torch.float32)])
+def test_qkv_split_shapes_bit_exact(B, S, H, D, dtype):
+    """One-launch 16-byte path (head rows a multiple of 16 bytes) and the strided-copy fallback (D=60 fp16,
+    D=12 fp32 = 48 bytes: still 16-byte units)."""
+    ops = _ops()
+    qkv = torch.randn(B, S, 3 * H * D).to(dtype)
+    q, k, v = ops.qkv_split(qkv.cuda(), H)
+    rq, rk, rv = oracle.qkv_split(qkv, H)
+    assert torch.equal(q.cpu(), rq) and torch.equal(k.cpu(), rk) and torch.equal(v.cpu(), rv)
+    assert ops.device_error() == 0
+
+
 def test_library_rejects_bad_arguments_on_gpu():
     from lunara_b200.runtime import _lib
     ops = _ops()
