@@ -42,17 +42,23 @@ struct StridedDesc {
   int64_t strides[kMaxDims];  // in units
 };
 
-template <typename U>
+// IdxT is uint32_t when the element count fits (32-bit division is several
+// times cheaper than 64-bit on the SM), else int64_t; source offsets stay
+// 64-bit either way.
+template <typename U, typename IdxT>
 __global__ void __launch_bounds__(kThreads) copy_strided_kernel(const U* __restrict__ src, U* __restrict__ dst,
                                                                 StridedDesc d, int64_t total) {
-  const int64_t step = static_cast<int64_t>(gridDim.x) * kThreads;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < total; i += step) {
-    int64_t rem = i, off = 0;
+  const IdxT step = static_cast<IdxT>(gridDim.x) * kThreads;
+  const IdxT n = static_cast<IdxT>(total);
+  for (IdxT i = static_cast<IdxT>(blockIdx.x) * kThreads + threadIdx.x; i < n; i += step) {
+    IdxT rem = i;
+    int64_t off = 0;
 #pragma unroll
     for (int k = kMaxDims - 1; k >= 0; --k) {
       if (k < d.ndim) {
-        const int64_t q = rem / d.sizes[k];
-        off += (rem - q * d.sizes[k]) * d.strides[k];
+        const IdxT sz = static_cast<IdxT>(d.sizes[k]);
+        const IdxT q = rem / sz;
+        off += static_cast<int64_t>(rem - q * sz) * d.strides[k];
         rem = q;
       }
     }
@@ -114,7 +120,12 @@ cudaError_t copy_u(const void* src, void* dst, const StridedDesc& d, int64_t tot
   const int64_t need = ceil_div64(total, kThreads);
   const int64_t cap = int64_t{device_num_sms()} * 16;
   const unsigned grid = static_cast<unsigned>(need < cap ? (need < 1 ? 1 : need) : cap);
-  copy_strided_kernel<U><<<grid, kThreads, 0, s>>>(static_cast<const U*>(src), static_cast<U*>(dst), d, total);
+  if (total + int64_t{grid} * kThreads < (int64_t{1} << 32))
+    copy_strided_kernel<U, uint32_t><<<grid, kThreads, 0, s>>>(static_cast<const U*>(src), static_cast<U*>(dst), d,
+                                                                total);
+  else
+    copy_strided_kernel<U, int64_t><<<grid, kThreads, 0, s>>>(static_cast<const U*>(src), static_cast<U*>(dst), d,
+                                                               total);
   return cudaGetLastError();
 }
 
