@@ -7,7 +7,7 @@ sm_100a kernels captured in one CUDA graph. A step is one forward of that block
 over 4096 tokens; metric = encoder-block tokens/s.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl lunara|reference]
-                  [--workload block|stack|gemm|attention|attention_causal|layernorm|bias_gelu|softmax|qkv_split]
+                  [--workload block|stack|gemm|attention|attention_causal|layernorm|bias_gelu|softmax|qkv_split|tp_ffn]
 
 Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events on
 the launching stream, with a 256 MB L2-flush write between steps (outside the
@@ -337,7 +337,7 @@ def main():
     ap.add_argument("--impl", choices=["lunara", "reference"], default="lunara")
     ap.add_argument("--workload", default="block",
                     choices=["block", "stack", "gemm", "attention", "attention_causal", "layernorm", "bias_gelu",
-                             "softmax", "qkv_split"])
+                             "softmax", "qkv_split", "tp_ffn"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     assert args.warmup >= 0 and args.steps >= 1

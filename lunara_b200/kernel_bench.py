@@ -216,6 +216,68 @@ def run(workload, args, rank, world, device):
                     roofline={"bound": "tensor", "achieved": ach, "peak": tflops_peak * world,
                               "unit": "TFLOP/s", "frac": ach / (tflops_peak * world),
                               "peak_source": f"{src} bf16 burst x {world} GPUs"})
+    elif workload == "tp_ffn":
+        line.update(_tp_ffn(args, rank, world, device, tflops_peak, src))
     else:
         raise ValueError(workload)
     return line
+
+
+def _tp_ffn(args, rank, world, device, tflops_peak, src):
+    """One tensor-parallel encoder layer over B64 S512 (32768 tokens): attention
+    replicated on every rank, FFN W1 column-split / W2 row-split over ``world``
+    ranks, one NCCL all-reduce (sum) of the [32768, 768] fp16 partials per layer.
+
+    Eager launches (every kernel here runs for tens of microseconds or more, so
+    host launch cost stays hidden); CUDA events around ``steps`` layers after a
+    barrier, max over ranks. Working set (x 50 MB, QKV 151 MB, ...) exceeds L2.
+    The all-reduce alone is timed the same way for its bus bandwidth.
+    """
+    import torch.distributed as dist
+    from oracle import inputs
+    from lunara_b200.runtime.sharding import TPEncoderBlock
+    x, ws = inputs.stack_inputs(batch=64, seq=512, layers=1, seed=4)
+    allreduce = None if world > 1 else (lambda t: None)
+    blk = TPEncoderBlock(ws[0], batch=64, seq=512, num_heads=12, world=world, rank=rank, device=device,
+                         allreduce=allreduce)
+    blk.x.copy_(x.half().reshape(-1, 768).to(device))
+    stream = torch.cuda.current_stream()
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(steps):
+            fn()
+        e.record(stream)
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e)
+        if world > 1:
+            tt = torch.tensor([ms], dtype=torch.float64, device=device)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms = float(tt.item())
+        return ms / steps
+
+    steps = min(args.steps, 200)
+    layer_ms = timed(blk.run_kernels, steps)
+    ar_ms = timed(lambda: blk.allreduce(blk.g), steps) if world > 1 else 0.0
+    tokens = 64 * 512
+    ffn_flops = 2.0 * 2 * tokens * 768 * 3072
+    rank_flops = 8 * (64.42e9 - 38.66e9) + ffn_flops / world   # replicated attention part + FFN shard
+    ach = rank_flops / (layer_ms * 1e-3) / 1e12
+    ar_bytes = tokens * 768 * 2
+    bus = (2.0 * (world - 1) / world * ar_bytes / (ar_ms * 1e-3) / 1e9) if world > 1 else None
+    return dict(metric="tensor-parallel FFN encoder layer tokens/s (B64,S512,H768)",
+                value=tokens / (layer_ms * 1e-3), unit="tokens/s", dtype="f16", scaling="strong",
+                ms_per_step=layer_ms, steps=steps,
+                config={"workload": "encoder layer B64 S512 fp16, FFN split over ranks, NCCL all-reduce",
+                        "global_batch": 64, "parallelism": f"tp-ffn x{world}", "l2": "working set > L2"},
+                allreduce={"ms": ar_ms, "bytes": ar_bytes, "bus_gbs": bus,
+                           "share_of_layer": (ar_ms / layer_ms) if world > 1 else 0.0},
+                roofline={"bound": "tensor", "achieved": ach, "peak": tflops_peak, "unit": "TFLOP/s per rank",
+                          "frac": ach / tflops_peak, "peak_source": f"{src} bf16 burst"})
