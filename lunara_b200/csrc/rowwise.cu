@@ -11,7 +11,8 @@
 // variance in fp32, then (x - mean) / sqrt(var + eps) * w + b), with the
 // variance taken over exactly N elements: the reference also sums (0 - mean)^2
 // for the padding lanes of its power-of-two block, which is not kept.
-// Softmax follows triton_emitter.py:341-353 (max, exp(x - max), / sum).
+// Softmax follows triton_emitter.py:341-353 (max, exp(x - max), / sum; the
+// division taken as one reciprocal per row and a multiply per element).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -225,7 +226,10 @@ __global__ void __launch_bounds__(kWarpRowThreads) softmax_warp_kernel(const T* 
       }
     }
   }
-  sum = warp_sum(sum);
+  // One division per row, then a multiply per element: an IEEE division per
+  // element made this kernel ALU-bound (49152 x 512 fp16: 21.5 us, against
+  // 17.2 us with the reciprocal, which is what a plain copy of the rows takes).
+  const float rsum = 1.0f / warp_sum(sum);
   uint4* yr = reinterpret_cast<uint4*>(Y + row * N);
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
@@ -233,7 +237,7 @@ __global__ void __launch_bounds__(kWarpRowThreads) softmax_warp_kernel(const T* 
     if (vi < nv) {
       float o[EPV];
 #pragma unroll
-      for (int e = 0; e < EPV; ++e) o[e] = v[i][e] / sum;
+      for (int e = 0; e < EPV; ++e) o[e] = v[i][e] * rsum;
       yr[vi] = pack_vec<T>(o);
     }
   }
@@ -251,10 +255,10 @@ __global__ void __launch_bounds__(kRowThreads) softmax_block_kernel(const T* __r
   const float mxs = mx * kLog2e;
   float s = 0.f;
   for (int64_t c = threadIdx.x; c < N; c += kRowThreads) s += ex2_approx(fmaf(Io<T>::to_f(xr[c]), kLog2e, -mxs));
-  s = block_sum<kRowThreads>(s, red);
+  const float rs = 1.0f / block_sum<kRowThreads>(s, red);
   T* yr = Y + row * N;
   for (int64_t c = threadIdx.x; c < N; c += kRowThreads)
-    yr[c] = Io<T>::from_f(ex2_approx(fmaf(Io<T>::to_f(xr[c]), kLog2e, -mxs)) / s);
+    yr[c] = Io<T>::from_f(ex2_approx(fmaf(Io<T>::to_f(xr[c]), kLog2e, -mxs)) * rs);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
