@@ -35,6 +35,16 @@ def _peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def _sustained_tflops() -> float:
+    """cuBLAS bf16 throughput held for seconds under the 1 kW power cap: the
+    denominator for a GEMM loop that itself runs for seconds."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("bf16_tflops_sustained", d["bf16_tflops"])
+    return 1400.0
+
+
 def _time_steps(fns, steps, warmup, flush):
     """Per-launch device time (ms), one value per step.
 
@@ -107,8 +117,11 @@ def run(workload, args, rank, world, device):
         line.update(metric="GEMM 4096^3 fp16 TFLOP/s", value=tp, unit="TFLOP/s", dtype="f16",
                     config={"workload": "GEMM M=N=K=4096 fp16 row-major, fp32 accumulate"},
                     ms_per_step=statistics.median(t_plain), bias_gelu_tflops=tf,
+                    timed_seconds=sum(t_plain) * 10 * 1e-3,
                     roofline={"bound": "tensor", "achieved": tp, "peak": tflops_peak, "unit": "TFLOP/s",
-                              "frac": tp / tflops_peak, "peak_source": f"{src} bf16 burst"})
+                              "frac": tp / tflops_peak, "peak_source": f"{src} bf16 burst",
+                              "sustained_peak": _sustained_tflops(),
+                              "frac_of_sustained": tp / _sustained_tflops()})
     elif workload in ("attention", "attention_causal"):
         causal = workload == "attention_causal"
         q, k, v = (t.half().to(device) for t in inputs.attention_inputs())
