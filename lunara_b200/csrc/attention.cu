@@ -55,8 +55,11 @@ constexpr float kRescaleLog2 = 8.0f;
 // Of the 16 exponential pairs in each 32-column chunk, kPolyPairs are computed
 // by a cubic on the f32x2 FMA pipe and the rest by MUFU ex2 (16 results per
 // clock per SM), so the two pipes share the softmax's exponentials.
+// 4 of 16 measured fastest on B200 with the persistent kernel (B2 H12 S2048:
+// 47.9 us against 49.6 with none, 49.0 with 6 and 53.9 with 8; the block
+// shape B8 H12 S512: 19.3 against 19.7 us).
 #ifndef LUNARA_ATTN_POLY_PAIRS
-#define LUNARA_ATTN_POLY_PAIRS 0
+#define LUNARA_ATTN_POLY_PAIRS 4
 #endif
 constexpr int kPolyPairs = LUNARA_ATTN_POLY_PAIRS;
 static_assert(kPolyPairs >= 0 && kPolyPairs <= 16, "poly pairs per chunk");
@@ -710,4 +713,34 @@ cudaError_t launch_attention_simt(const AttnArgs& a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+namespace {
+// y[i] = 2^x[i] by the FMA-pipe exponential of the attention softmax: the
+// scalar ex2_poly (pair == 0) or the f32x2 ex2_poly2 on (x[2i], x[2i+1]).
+__global__ void ex2_poly_selftest_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n, int pair) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (pair) {
+    if (2 * i + 1 >= n) return;
+    const float2 r = f2_unpack(ex2_poly2(f2_pack(x[2 * i], x[2 * i + 1])));
+    y[2 * i] = r.x;
+    y[2 * i + 1] = r.y;
+  } else if (i < n) {
+    y[i] = ex2_poly(x[i]);
+  }
+}
+}  // namespace
+
 }  // namespace lunara
+
+// Internal self-test entry point (not part of the public C ABI in
+// include/lunara_b200.h): evaluates the attention softmax's FMA-pipe 2^x over
+// n device floats so that tests can bound its error against exp2. n must be
+// even when pair != 0. Returns 0, or 1 for bad arguments, 3 for a launch error.
+extern "C" __attribute__((visibility("default"))) int lunara_selftest_ex2_poly(const float* x, float* y, int64_t n,
+                                                                             int pair, void* stream) {
+  if (n < 0 || (n > 0 && (x == nullptr || y == nullptr)) || (pair && (n & 1)) || n > (int64_t{1} << 30)) return 1;
+  if (n == 0) return 0;
+  const int64_t threads = pair ? n / 2 : n;
+  const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
+  lunara::ex2_poly_selftest_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n, pair);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
