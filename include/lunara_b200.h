@@ -159,7 +159,13 @@ const char* lunara_last_error_string(void);
 
 /* Synchronizes `stream`, then returns the device error word (0 = none) and
  * clears it when `clear` is non-zero. Codes: 0x1xx GEMM, 0x2xx attention
- * (a bounded wait ran out), 0x301 gather index out of range. */
+ * (a bounded wait ran out), 0x301 gather index out of range, 0x4xx the
+ * self-tests of lunara_b200_selftest.h.
+ * The word is one per device and sticky: a kernel on any stream of the
+ * current device sets it (the first failure wins) and it stays set until a
+ * caller clears it. Only `stream` is synchronized, so a caller that launched
+ * on several streams synchronizes all of them (or the device) first; two
+ * threads reading and clearing it at the same time may both see one error. */
 int lunara_device_error(void* stream, int clear);
 
 /* Number of SMs of the current device, as the kernels size their grids. */

@@ -1,0 +1,34 @@
+/*
+ * lunara_b200_selftest.h -- internal self-test entry points of liblunara_b200.so.
+ *
+ * These are not part of the kernel ABI in lunara_b200.h and have no
+ * counterpart in the reference: they exist so that tests can check device
+ * code paths that no product input reaches on purpose. Both return 0 on
+ * success, 1 for bad arguments and 3 when the launch failed.
+ */
+#ifndef LUNARA_B200_SELFTEST_H
+#define LUNARA_B200_SELFTEST_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* y[i] = 2^x[i] over n device floats by the attention softmax's FMA-pipe
+ * exponential: the scalar form (pair == 0) or the f32x2 form on pairs
+ * (pair != 0, n even). Lets tests bound its error against exp2. */
+int lunara_selftest_ex2_poly(const float* x, float* y, int64_t n, int pair, void* stream);
+
+/* Launches one CTA that waits on an mbarrier nothing ever arrives on, with a
+ * %globaltimer budget of budget_ns (1 us .. 1 s), exactly as the product
+ * kernels bound every wait. When the budget runs out the kernel records
+ * `site` (0x401 .. 0x4ff) in the device error word and returns; nothing
+ * faults or hangs. Read the outcome with lunara_device_error(). */
+int lunara_selftest_bounded_wait(uint64_t budget_ns, unsigned int site, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LUNARA_B200_SELFTEST_H */

@@ -203,7 +203,11 @@ int lunara_attention(const void* Q, const void* K, const void* V, void* O, int64
   a.causal = causal ? 1 : 0;
   a.dtype = dtype;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (attention_tc_supported(a)) return from_cuda(launch_attention_tcgen05(a, s), "lunara_attention(tcgen05)");
+  if (attention_tc_supported(a)) {
+    bool handled = false;
+    const cudaError_t e = launch_attention_tcgen05(a, s, &handled);
+    if (handled) return from_cuda(e, "lunara_attention(tcgen05)");
+  }
   return from_cuda(launch_attention_simt(a, s), "lunara_attention(simt)");
 }
 
@@ -267,7 +271,10 @@ int lunara_gather(const void* src, const int64_t* index, void* dst, int64_t n_in
   if (n_index == 0 || row_bytes == 0) return ok();
   if (!index || !dst) return fail(LUNARA_ERR_INVALID_ARG, "lunara_gather: NULL pointer");
   if (!src && src_rows > 0) return fail(LUNARA_ERR_INVALID_ARG, "lunara_gather: NULL source");
-  if (n_index >= (int64_t{1} << 34)) return fail(LUNARA_ERR_UNSUPPORTED, "lunara_gather: too many indices");
+  // One warp per row, 8 rows per 256-thread block: the grid's x dimension
+  // (at most 2^31 - 1 blocks) bounds the row count.
+  if (n_index > int64_t{8} * ((int64_t{1} << 31) - 1))
+    return fail(LUNARA_ERR_UNSUPPORTED, "lunara_gather: too many indices");
   return from_cuda(launch_gather(src, index, dst, n_index, src_rows, row_bytes, static_cast<cudaStream_t>(stream)),
                    "lunara_gather");
 }

@@ -627,20 +627,40 @@ bool encode_4d(CUtensorMap* map, const void* base, int dtype, int64_t S, int64_t
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool strides_ok(const int64_t* s) {
-  // dim stride 1; batch/head/seq strides give 16-byte aligned rows and fit TMA's 40-bit stride field.
+// Strides of a [B, H, S, D] view as the tensor map takes them: a dimension of
+// extent 1 is never stepped, so whatever stride torch gives it (0 after an
+// expand, anything after a slice) is replaced by a harmless 16-byte multiple.
+void map_strides(const int64_t* st, int64_t B, int64_t H, int64_t S, int64_t (&out)[4]) {
+  const int64_t ext[3] = {B, H, S};
+  for (int i = 0; i < 3; ++i) out[i] = ext[i] == 1 ? kHeadDim : st[i];
+  out[3] = st[3];
+}
+
+bool strides_ok(const int64_t* st, int64_t B, int64_t H, int64_t S) {
+  // Dim stride 1; each stepped batch / head / seq stride positive (a zero
+  // stride, e.g. K/V expanded over the batch, goes to the CUDA-core kernel),
+  // a multiple of 16 bytes and within TMA's 40-bit stride field.
+  int64_t s[4];
+  map_strides(st, B, H, S, s);
   if (s[3] != 1) return false;
   for (int i = 0; i < 3; ++i)
-    if (s[i] < 0 || (s[i] * 2) % 16 != 0 || s[i] * 2 >= (int64_t{1} << 40)) return false;
+    if (s[i] <= 0 || (s[i] * 2) % 16 != 0 || s[i] * 2 >= (int64_t{1} << 40)) return false;
   return true;
 }
 
 template <typename T>
-cudaError_t run_tc(const AttnArgs& a, cudaStream_t s) {
+cudaError_t run_tc(const AttnArgs& a, cudaStream_t s, bool* handled) {
   CUtensorMap mq, mk, mv;
-  if (!encode_4d(&mq, a.Q, a.dtype, a.Sq, a.H, a.B, a.qs) || !encode_4d(&mk, a.K, a.dtype, a.Skv, a.H, a.B, a.ks) ||
-      !encode_4d(&mv, a.V, a.dtype, a.Skv, a.H, a.B, a.vs))
-    return cudaErrorInvalidValue;
+  int64_t qs[4], ks[4], vs[4];
+  map_strides(a.qs, a.B, a.H, a.Sq, qs);
+  map_strides(a.ks, a.B, a.H, a.Skv, ks);
+  map_strides(a.vs, a.B, a.H, a.Skv, vs);
+  if (!encode_4d(&mq, a.Q, a.dtype, a.Sq, a.H, a.B, qs) || !encode_4d(&mk, a.K, a.dtype, a.Skv, a.H, a.B, ks) ||
+      !encode_4d(&mv, a.V, a.dtype, a.Skv, a.H, a.B, vs)) {
+    *handled = false;   // the driver refused a tensor map: the CUDA-core kernel takes the call
+    return cudaSuccess;
+  }
+  *handled = true;
   auto kern = attn_tc_kernel<T>;
   // The setmaxnreg split assumes the kernel launches with exactly kLaunchRegs
   // registers per thread; refuse to launch a build where that does not hold.
@@ -680,12 +700,16 @@ bool attention_tc_supported(const AttnArgs& a) {
   if (a.Sq < 1 || a.Skv < 1 || a.Sq >= (int64_t{1} << 30) || a.Skv >= (int64_t{1} << 30)) return false;
   if (a.H > 65535 || a.B > 65535) return false;
   if (!al16(a.Q) || !al16(a.K) || !al16(a.V) || !al16(a.O)) return false;
-  if (!strides_ok(a.qs) || !strides_ok(a.ks) || !strides_ok(a.vs) || !strides_ok(a.os)) return false;
+  if (!strides_ok(a.qs, a.B, a.H, a.Sq) || !strides_ok(a.ks, a.B, a.H, a.Skv) || !strides_ok(a.vs, a.B, a.H, a.Skv))
+    return false;
+  if (a.os[3] != 1) return false;   // O is written with plain 16-byte stores: unit dim stride, aligned rows
+  for (int i = 0; i < 3; ++i)
+    if ((a.os[i] * 2) % 16 != 0) return false;
   return true;
 }
 
-cudaError_t launch_attention_tcgen05(const AttnArgs& a, cudaStream_t stream) {
-  return a.dtype == LUNARA_BF16 ? run_tc<__nv_bfloat16>(a, stream) : run_tc<__half>(a, stream);
+cudaError_t launch_attention_tcgen05(const AttnArgs& a, cudaStream_t stream, bool* handled) {
+  return a.dtype == LUNARA_BF16 ? run_tc<__nv_bfloat16>(a, stream, handled) : run_tc<__half>(a, stream, handled);
 }
 
 cudaError_t launch_attention_simt(const AttnArgs& a, cudaStream_t stream) {
@@ -713,34 +737,4 @@ cudaError_t launch_attention_simt(const AttnArgs& a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-namespace {
-// y[i] = 2^x[i] by the FMA-pipe exponential of the attention softmax: the
-// scalar ex2_poly (pair == 0) or the f32x2 ex2_poly2 on (x[2i], x[2i+1]).
-__global__ void ex2_poly_selftest_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n, int pair) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (pair) {
-    if (2 * i + 1 >= n) return;
-    const float2 r = f2_unpack(ex2_poly2(f2_pack(x[2 * i], x[2 * i + 1])));
-    y[2 * i] = r.x;
-    y[2 * i + 1] = r.y;
-  } else if (i < n) {
-    y[i] = ex2_poly(x[i]);
-  }
-}
-}  // namespace
-
 }  // namespace lunara
-
-// Internal self-test entry point (not part of the public C ABI in
-// include/lunara_b200.h): evaluates the attention softmax's FMA-pipe 2^x over
-// n device floats so that tests can bound its error against exp2. n must be
-// even when pair != 0. Returns 0, or 1 for bad arguments, 3 for a launch error.
-extern "C" __attribute__((visibility("default"))) int lunara_selftest_ex2_poly(const float* x, float* y, int64_t n,
-                                                                             int pair, void* stream) {
-  if (n < 0 || (n > 0 && (x == nullptr || y == nullptr)) || (pair && (n & 1)) || n > (int64_t{1} << 30)) return 1;
-  if (n == 0) return 0;
-  const int64_t threads = pair ? n / 2 : n;
-  const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
-  lunara::ex2_poly_selftest_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n, pair);
-  return cudaGetLastError() == cudaSuccess ? 0 : 3;
-}

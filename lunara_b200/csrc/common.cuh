@@ -33,6 +33,7 @@ enum DeviceErrorSite : unsigned int {
   kErrAttnMma = 0x202,
   kErrAttnSoftmax = 0x203,
   kErrGatherIndex = 0x301,
+  kErrSelftestWait = 0x401,   // the bounded-wait self-test kernel (never set by a product kernel)
 };
 
 // Budget for one mbarrier wait: 4 s of %globaltimer. A correct kernel waits
@@ -102,15 +103,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for the phase with the given parity to complete.
 // Returns false when the CTA is aborting (this wait or another one ran out).
+// `budget_ns` is the %globaltimer budget of this wait (kWaitBudgetNs in every
+// product kernel; the self-test passes a short one).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          unsigned int* err, unsigned int site) {
+                                          unsigned int* err, unsigned int site,
+                                          unsigned long long budget_ns = kWaitBudgetNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 3u) == 0u) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+      if (globaltimer_ns() - t0 > budget_ns) {
         *abort_flag = 1;
         atomicCAS(err, 0u, site);
         return false;
@@ -341,6 +345,73 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// ------------------------------------------- clusters of more than two CTAs --
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t nclusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the variable at the same offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t local_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+  return r;
+}
+
+// Asynchronous 8-byte store into (possibly another CTA's) shared memory that
+// completes 8 transaction bytes on the mbarrier at `remote_bar` in the same
+// CTA as the destination.
+__device__ __forceinline__ void st_async_v2_f32(uint32_t remote_addr, float a, float b, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+                   remote_addr),
+               "f"(a), "f"(b), "r"(remote_bar)
+               : "memory");
+}
+
+// try_wait whose acquire covers writes made by other CTAs of the cluster.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait (as mbar_wait) with cluster-scope acquire.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                  unsigned int* err, unsigned int site) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((it & 3u) == 0u) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+        *abort_flag = 1;
+        atomicCAS(err, 0u, site);
+        return false;
+      }
+    }
+  }
+}
+
 // Warpgroup-wide register budget changes (all warps of the warpgroup execute
 // the same one). The sum over the CTA must stay within the launch allocation.
 template <int N>
@@ -426,16 +497,23 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // adding 1.5 * 2^23 so that the integer lands in the low mantissa bits, and
 // f in [-0.5, 0.5]; 2^f by a cubic fitted here to minimise relative error on
 // that interval (max relative error 7.5e-5); 2^j by adding j to the exponent
-// field. Inputs below -126 are clamped (results below 2^-126 are not needed).
+// field. The polynomial runs on x clamped to >= -126; the result is then
+// corrected to what MUFU ex2.approx.ftz returns outside that range: exactly 0
+// below -126 (a subnormal result is flushed, so a masked -inf score gives a
+// zero probability in every dtype) and NaN for a NaN input.
+__device__ __forceinline__ float ex2_fix_range(float x, float r) {
+  return x >= -126.0f ? r : (x < -126.0f ? 0.0f : x);
+}
+
 __device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -126.0f);
-  const float t = x + 12582912.0f;
-  const float f = x - (t - 12582912.0f);
+  const float xc = fmaxf(x, -126.0f);
+  const float t = xc + 12582912.0f;
+  const float f = xc - (t - 12582912.0f);
   float p = fmaf(0.0551716685f, f, 0.2426111400f);
   p = fmaf(p, f, 0.6932609677f);
   p = fmaf(p, f, 0.9999280572f);
   const int j = __float_as_int(t) - 0x4B400000;
-  return __int_as_float(__float_as_int(p) + (j << 23));
+  return ex2_fix_range(x, __int_as_float(__float_as_int(p) + (j << 23)));
 }
 
 // Pairs of fp32 values in one 64-bit register pair, for the sm_100 f32x2
@@ -488,8 +566,8 @@ __device__ __forceinline__ uint64_t ex2_poly2(uint64_t x2) {
   p = f2_fma(p, f, f2_pack(0.9999280572f, 0.9999280572f));
   const float2 tv = f2_unpack(t), pv = f2_unpack(p);
   // (bits(t) - bits(1.5 * 2^23)) << 23 == bits(t) << 23 modulo 2^32.
-  return f2_pack(__uint_as_float(__float_as_uint(pv.x) + (__float_as_uint(tv.x) << 23)),
-                 __uint_as_float(__float_as_uint(pv.y) + (__float_as_uint(tv.y) << 23)));
+  return f2_pack(ex2_fix_range(x.x, __uint_as_float(__float_as_uint(pv.x) + (__float_as_uint(tv.x) << 23))),
+                 ex2_fix_range(x.y, __uint_as_float(__float_as_uint(pv.y) + (__float_as_uint(tv.y) << 23))));
 }
 
 __device__ __forceinline__ float tanh_approx(float x) {

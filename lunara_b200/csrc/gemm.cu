@@ -1,21 +1,23 @@
 // GEMM with fused epilogue: C = act(A * B + bias) + residual.
 //
-// tcgen05 path (f16 / bf16, TMA-compatible strides):
-//   persistent, warp-specialised kernel, one CTA per SM, 320 threads
+// tcgen05 path (f16 / bf16, TMA-compatible strides): persistent,
+// warp-specialised kernels with one CTA per SM and 448 threads (14 warps):
 //     warp 0      TMA producer: A [128 x 64] and B [BN x 64] tiles, 128-byte
 //                 swizzle, into a STAGES-deep shared-memory ring
 //     warp 1      TMEM allocator + single-thread tcgen05.mma issuer
 //                 (M=128, N=BN, K=16 per instruction, fp32 accumulate)
-//     warps 2..9  epilogue (two warps per TMEM lane quarter, half the columns
-//                 each): tcgen05.ld of the accumulator one 32-column chunk
-//                 ahead (thread = row), bias (staged per warp in shared
-//                 memory) + activation + residual (loaded one chunk ahead) in
-//                 fp32, one rounding; each warp stages its 32 x 32 output
-//                 chunk in shared memory (64-byte swizzle) and writes it with
-//                 one TMA store (direct 16-byte stores when C is unaligned)
+//     warps 2..13 epilogue, three warps per TMEM lane quarter (warp % 4): the
+//                 tile's 32-column chunks are dealt to the three round-robin;
+//                 each chunk is read from TMEM (thread = row), gets bias
+//                 (staged per warp in shared memory) + activation + residual
+//                 (loaded one chunk ahead) in fp32 with one rounding, is staged
+//                 as a 32 x 32 tile in shared memory (64-byte swizzle) and
+//                 written by one TMA store (direct 16-byte stores when C is
+//                 unaligned)
 //   Two TMEM accumulators (2 x BN fp32 columns) let the epilogue of tile i
-//   overlap the main loop of tile i+1. No TMA multicast is used anywhere (the
-//   same kernel runs in multi-GPU jobs).
+//   overlap the main loop of tile i+1. gemm_tc2_kernel runs the same roles on
+//   a CTA pair (cta_group::2, 256-row tiles). No TMA multicast is used
+//   anywhere (the same kernels run in multi-GPU jobs).
 // SIMT path: any shape / stride / dtype (incl. f32), 64x64 register tiles.
 //
 // Semantics follow the reference GEMM template,
@@ -26,6 +28,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -897,13 +900,22 @@ cudaError_t run_tc2(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap&
                                        kMaxStages * kStageBytes + kSmemReserve);
   if (e != cudaSuccess) return e;
   // Persistent grid: as many CTA pairs as can be resident (clusters of two
-  // need both SMs of a pair free), capped by the number of 256-row tiles.
-  static int cached_clusters[64] = {};   // per device, for this kernel instantiation
+  // need both SMs of a pair free), capped by the number of 256-row tiles. The
+  // occupancy query depends on the shared-memory size, so its answer is cached
+  // per device and ring depth, under a lock.
+  static std::mutex cache_mu;
+  static int cached_clusters[64][9] = {};   // [device][stages], for this kernel instantiation
   int dev = 0;
-  cudaGetDevice(&dev);
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
   int max_clusters = device_num_sms() / 2;
-  if (dev >= 0 && dev < 64 && cached_clusters[dev] > 0) {
-    max_clusters = cached_clusters[dev];
+  const bool cacheable = dev >= 0 && dev < 64 && stages >= 0 && stages < 9;
+  int cached = 0;
+  if (cacheable) {
+    std::lock_guard<std::mutex> lk(cache_mu);
+    cached = cached_clusters[dev][stages];
+  }
+  if (cached > 0) {
+    max_clusters = cached;
   } else {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(2 * max_clusters));
@@ -914,7 +926,10 @@ cudaError_t run_tc2(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap&
     if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0 && n < max_clusters)
       max_clusters = n;
     cudaGetLastError();
-    if (dev >= 0 && dev < 64) cached_clusters[dev] = max_clusters;
+    if (cacheable) {
+      std::lock_guard<std::mutex> lk(cache_mu);
+      cached_clusters[dev][stages] = max_clusters;
+    }
   }
   const int64_t tiles = ceil_div64(g.M, 2 * BM) * ceil_div64(g.N, BN);
   int64_t clusters = g.num_ctas > 1 ? g.num_ctas / 2 : max_clusters;

@@ -91,7 +91,9 @@ struct AttnArgs {
 };
 
 bool attention_tc_supported(const AttnArgs& a);
-cudaError_t launch_attention_tcgen05(const AttnArgs& a, cudaStream_t stream);
+// Sets *handled to false (and launches nothing) when the driver refuses one of
+// the tensor maps; the caller then runs the CUDA-core kernel.
+cudaError_t launch_attention_tcgen05(const AttnArgs& a, cudaStream_t stream, bool* handled);
 cudaError_t launch_attention_simt(const AttnArgs& a, cudaStream_t stream);
 
 // Resolves cuTensorMapEncodeTiled through the runtime's driver entry point

@@ -51,10 +51,11 @@ class CompiledModel:
 
     def _apply_tuning(self) -> None:
         # Tuned GEMM tiles replace the emitted defaults (same effect as re-emitting).
+        from lunara_b200.codegen.autotuner import gemm_call_args
         for name, res in self.tuning_results.items():
             key = f"_TILE_{name}"
             if key in self._ns and res is not None:
-                self._ns[key].update(block_n=res.config.BLOCK_N, stages=res.config.num_stages)
+                self._ns[key].update(gemm_call_args(res.config))
 
     def get_launch_fn(self, name: str):
         fn = self._ns.get(f"{name}_launch")

@@ -97,6 +97,65 @@ def _same_size_copy_gbs(nbytes: int, steps: int, warmup: int, flush, device) -> 
     return 2.0 * words * 8 / (statistics.median(t) * 1e-3) / 1e9
 
 
+def config_kernel_map(device, steps: int = 20, warmup: int = 3):
+    """Every single-kernel benchmark configuration, timed as the workloads above
+    (rotated buffer sets, 256 MB flush between steps, graphs of 10 launches),
+    with a short step count: {name: {ms, value, unit, frac, peak_source}}.
+
+      gemm4096_{f16,bf16}[_bias_gelu]   M=N=K=4096, tensor roof
+      attention_s2048[_causal]          B2 H12 S2048 D64 fp16, tensor roof (causal: half the FLOPs)
+      layernorm_16384x768               fp16, HBM roof
+      bias_gelu_16384x3072              fp16, HBM roof
+    """
+    from oracle import inputs
+    from lunara_b200.runtime import ops
+    hbm, tflops_peak, src = _peaks()
+    flush = torch.empty(32 << 20, dtype=torch.int64, device=device)
+    out = {}
+
+    def put(name, t, work, unit):
+        ms = statistics.median(t)
+        if unit == "TFLOP/s":
+            val, peak = work / (ms * 1e-3) / 1e12, tflops_peak
+        else:
+            val, peak = work / (ms * 1e-3) / 1e9, hbm
+        out[name] = {"ms": round(ms, 5), "value": round(val, 1), "unit": unit, "frac": round(val / peak, 3),
+                     "peak_source": f"{src} {'bf16 burst' if unit == 'TFLOP/s' else 'copy'}"}
+
+    a, b, bias = inputs.gemm_inputs()
+    for dt, tag in ((torch.float16, "f16"), (torch.bfloat16, "bf16")):
+        ad, bd, biasd = a.to(dt).to(device), b.to(dt).to(device), bias.to(dt).to(device)
+        sets = [(ad.clone(), bd.clone(), torch.empty(4096, 4096, dtype=dt, device=device))
+                for _ in range(_rotations(3 * 4096 * 4096 * 2))]
+        put(f"gemm4096_{tag}", _time_steps([lambda s=s_: ops.gemm(s[0], s[1], s[2]) for s_ in sets],
+                                           steps, warmup, flush), 2.0 * 4096 ** 3, "TFLOP/s")
+        put(f"gemm4096_{tag}_bias_gelu",
+            _time_steps([lambda s=s_: ops.gemm(s[0], s[1], s[2], bias=biasd, activation="gelu_tanh") for s_ in sets],
+                        steps, warmup, flush), 2.0 * 4096 ** 3, "TFLOP/s")
+        del sets, ad, bd
+    q, k, v = (t.half().to(device) for t in inputs.attention_inputs())
+    sets = [(q.clone(), k.clone(), v.clone(), torch.empty_like(q)) for _ in range(_rotations(4 * q.numel() * 2))]
+    for causal in (False, True):
+        t = _time_steps([lambda s=s_: ops.attention(s[0], s[1], s[2], causal=causal, out=s[3]) for s_ in sets],
+                        steps, warmup, flush)
+        put("attention_s2048" + ("_causal" if causal else ""), t,
+            4.0 * 2 * 12 * 2048 * 2048 * 64 * (0.5 if causal else 1.0), "TFLOP/s")
+    del sets
+    x, w, b = inputs.layernorm_inputs()
+    x, w, b = x.half().to(device), w.half().to(device), b.half().to(device)
+    sets = [(x.clone(), torch.empty_like(x)) for _ in range(_rotations(2 * x.numel() * 2))]
+    put("layernorm_16384x768", _time_steps([lambda s=s_: ops.layernorm(s[0], w, b, 1e-5, out=s[1]) for s_ in sets],
+                                           steps, warmup, flush), 2.0 * 16384 * 768 * 2 + 2 * 768 * 2, "GB/s")
+    del sets
+    x, bias = inputs.bias_gelu_inputs()
+    x, bias = x.half().to(device), bias.half().to(device)
+    sets = [(x.clone(), torch.empty_like(x)) for _ in range(_rotations(2 * x.numel() * 2))]
+    put("bias_gelu_16384x3072", _time_steps([lambda s=s_: ops.bias_act(s[0], bias, "gelu_tanh", out=s[1])
+                                             for s_ in sets], steps, warmup, flush),
+        2.0 * 16384 * 3072 * 2 + 3072 * 2, "GB/s")
+    return out
+
+
 def run(workload, args, rank, world, device):
     from oracle import inputs
     from lunara_b200.runtime import ops

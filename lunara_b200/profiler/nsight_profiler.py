@@ -10,9 +10,17 @@ nsight_profiler.py:36-379) with three changes:
   * the event profiler can flush L2 (a 256 MB write) between timed calls, so a
     working set that fits in the 126 MB L2 does not inflate HBM figures;
   * the ncu path really profiles the callable: it is serialised with
-    cloudpickle into a launcher script that ncu runs with ``--clock-control
-    none`` (the reference's launcher is a placeholder, 250-257), and the CSV
-    is parsed per kernel.
+    cloudpickle into a launcher script, which is first run once without ncu
+    (a call that fails there is never profiled) and then under ncu with
+    ``--clock-control none``, a kernel filter and a launch count (the
+    reference's launcher is a placeholder, 250-257); the CSV is parsed per
+    kernel;
+  * memory-bound kernels are graded on read + write bytes, and the report and
+    the roofline chart show each kernel against both roofs (HBM and tensor).
+
+``python -m lunara_b200.profiler.nsight_profiler --selfcheck`` profiles one
+small GEMM launch through the ncu path and compares its duration with the
+CUDA-event timing of the same launch.
 """
 from __future__ import annotations
 
@@ -42,17 +50,22 @@ class GPUSpec:
     shared_mem_per_sm: int   # bytes
 
 
+# Where each GPU's peak figures come from, for the report ("measured" or "datasheet").
+PEAK_SOURCE: Dict[str, str] = {}
+
+
 def _b200_spec() -> GPUSpec:
     """B200: measured peaks when MEASURED_PEAKS.json exists, else datasheet dense figures."""
-    fp16, hbm = 2250.0, 7.7
+    fp16, hbm, src = 2250.0, 7.7, "datasheet"
     for cand in (Path(os.environ.get("LUNARA_PEAKS", "")), Path(__file__).resolve().parents[2] / "MEASURED_PEAKS.json"):
         if cand.is_file():
             try:
                 d = json.loads(cand.read_text())
-                fp16, hbm = float(d["bf16_tflops"]), float(d["hbm_gbs"]) / 1000.0
+                fp16, hbm, src = float(d["bf16_tflops"]), float(d["hbm_gbs"]) / 1000.0, "measured"
             except (KeyError, ValueError):
                 pass
             break
+    PEAK_SOURCE["B200"] = src
     return GPUSpec("B200", fp16, 80.0, hbm, 20.0, 148, 228 * 1024)
 
 
@@ -117,14 +130,18 @@ class ProfileResult:
 
 def classify_roofline(m: KernelMetrics, flops: Optional[float], bytes_accessed: Optional[float],
                       gpu: GPUSpec) -> None:
-    """Memory- or compute-bound by arithmetic intensity vs the ridge point (nsight_profiler.py:161-171)."""
+    """Memory- or compute-bound by arithmetic intensity vs the ridge point (nsight_profiler.py:161-171).
+
+    A memory-bound kernel is graded on every byte it moves: read plus write
+    bandwidth against the HBM peak (a copy-like kernel writes as much as it reads).
+    """
     if flops is None or bytes_accessed is None or bytes_accessed <= 0:
         return
     m.arithmetic_intensity = flops / bytes_accessed
     ridge = gpu.peak_flops_fp16 / gpu.peak_bw_hbm   # FLOP per byte (TFLOPS / TB/s)
     if m.arithmetic_intensity < ridge:
         m.roofline_bound = "memory"
-        m.roofline_efficiency = m.hbm_read_bw_gbs / (gpu.peak_bw_hbm * 1000)
+        m.roofline_efficiency = (m.hbm_read_bw_gbs + m.hbm_write_bw_gbs) / (gpu.peak_bw_hbm * 1000)
     else:
         m.roofline_bound = "compute"
         m.roofline_efficiency = m.achieved_flops_t / gpu.peak_flops_fp16
@@ -167,6 +184,8 @@ class CUDAEventProfiler:
         if flops is not None:
             m.achieved_flops_t = flops / (med * 1e-6) / 1e12
         if bytes_accessed is not None and med > 0:
+            # Event timing sees no counters: the algorithmic bytes (reads and
+            # writes together) are reported as the read figure, the write figure stays 0.
             m.hbm_read_bw_gbs = bytes_accessed / (med * 1e-6) / 1e9
         classify_roofline(m, flops, bytes_accessed, gpu_spec)
         return m
@@ -202,12 +221,13 @@ class NsightProfiler:
     """Profile a callable with ncu (per-kernel metrics) or, without ncu, with CUDA events."""
 
     def __init__(self, ncu_path: str = "ncu", fallback_to_events: bool = True, launch_count: int = 8,
-                 kernel_regex: Optional[str] = None, warmup: int = 1):
+                 kernel_regex: Optional[str] = None, warmup: int = 1, metrics: Optional[List[str]] = None):
         self.ncu_path = ncu_path
         self.fallback = fallback_to_events
         self.launch_count = launch_count
         self.kernel_regex = kernel_regex
         self.warmup = warmup
+        self.metrics = list(metrics) if metrics else list(_NCU_METRICS)
         self._has_ncu = self._check_ncu()
         self.gpu_spec = detect_gpu()
         self._event_profiler = CUDAEventProfiler()
@@ -238,7 +258,7 @@ class NsightProfiler:
 
     def ncu_command(self, launcher: Path, csv_out: Path) -> List[str]:
         cmd = [self.ncu_path, "--clock-control", "none", "--csv", "--page", "raw",
-               "--metrics", ",".join(_NCU_METRICS), "--launch-skip", str(self.warmup),
+               "--metrics", ",".join(self.metrics), "--launch-skip", str(self.warmup),
                "--launch-count", str(self.launch_count), "--log-file", str(csv_out)]
         if self.kernel_regex:
             cmd += ["--kernel-name", f"regex:{self.kernel_regex}"]
@@ -253,6 +273,9 @@ class NsightProfiler:
             launcher = Path(tmp) / "launch.py"
             launcher.write_text(_LAUNCHER.format(paths=[p for p in sys.path if p], blob=str(blob)))
             csv_out = Path(tmp) / "metrics.csv"
+            # The same launcher runs once without ncu first: a call that fails (or
+            # faults) there is reported as an error and never profiled.
+            subprocess.run([sys.executable, str(launcher)], check=True, capture_output=True, timeout=300)
             subprocess.run(self.ncu_command(launcher, csv_out), check=True, capture_output=True, timeout=600)
             return self._parse_ncu_csv(csv_out, kernel_name, flops, bytes_accessed)
 
@@ -298,56 +321,105 @@ class NsightProfiler:
 
     @staticmethod
     def print_summary(result: ProfileResult) -> None:
-        sep = "─" * 60
-        print(f"\n{sep}")
-        print("  Lunara Kernel Profile Summary")
-        print(sep)
-        if result.gpu_spec:
-            g = result.gpu_spec
-            print(f"  GPU:  {g.name}  |  FP16 peak: {g.peak_flops_fp16:.0f} TFLOPS  |  HBM BW: {g.peak_bw_hbm:.1f} TB/s")
-        print()
-        for k in result.kernels:
-            print(f"  Kernel: {k.kernel_name}")
-            print(f"    Duration:    {k.duration_us:>10.2f} µs")
-            print(f"    SM util:     {k.sm_active_pct:>9.1f}%")
-            print(f"    Occupancy:   {k.achieved_occupancy * 100:>9.1f}%")
-            print(f"    HBM read BW: {k.hbm_read_bw_gbs:>9.1f} GB/s")
-            print(f"    Achieved:    {k.achieved_flops_t:>9.2f} TFLOPS")
-            print(f"    Arith. Int.: {k.arithmetic_intensity:>9.2f} FLOP/B")
-            print(f"    Roofline:    {k.roofline_bound:>9s} ({k.roofline_efficiency * 100:.1f}% of peak)")
-        print(sep + "\n")
+        """One table row per kernel: time, achieved TFLOP/s and HBM GB/s, each as a
+        fraction of its roof, and the roof that bounds the kernel."""
+        g = result.gpu_spec
+        rows = []
+        for k in sorted(result.kernels, key=lambda k: -k.duration_us):
+            hbm = k.hbm_read_bw_gbs + k.hbm_write_bw_gbs
+            tc_frac = k.achieved_flops_t / g.peak_flops_fp16 if g and g.peak_flops_fp16 else 0.0
+            bw_frac = hbm / (g.peak_bw_hbm * 1000.0) if g and g.peak_bw_hbm else 0.0
+            name = k.kernel_name if len(k.kernel_name) <= 34 else k.kernel_name[:31] + "..."
+            rows.append((name, f"{k.duration_us:.2f}", f"{k.achieved_flops_t:.1f}", f"{tc_frac:.2f}",
+                         f"{hbm:.0f}", f"{bw_frac:.2f}", f"{k.arithmetic_intensity:.1f}", k.roofline_bound))
+        head = ("kernel", "us", "TFLOP/s", "x tensor", "GB/s", "x HBM", "FLOP/B", "bound")
+        widths = [max(len(r[i]) for r in rows + [head]) for i in range(len(head))]
+        src = PEAK_SOURCE.get(g.name, "datasheet") if g else "-"
+        print(f"\nLunara Profile Summary -- {g.name if g else 'unknown GPU'}")
+        if g:
+            print(f"roofs ({src}): tensor {g.peak_flops_fp16:.0f} TFLOP/s, HBM {g.peak_bw_hbm * 1000:.0f} GB/s, "
+                  f"ridge {g.peak_flops_fp16 / g.peak_bw_hbm:.0f} FLOP/B")
+        line = "  ".join(h.rjust(w) if i else h.ljust(w) for i, (h, w) in enumerate(zip(head, widths)))
+        print(line)
+        print("-" * len(line))
+        for r in rows:
+            print("  ".join(c.rjust(w) if i else c.ljust(w) for i, (c, w) in enumerate(zip(r, widths))))
+        print(f"total {result.total_duration_us:.2f} us over {len(result.kernels)} kernel launch(es)\n")
 
     def plot_roofline(self, result: ProfileResult, output_path: str = "roofline.png") -> None:
-        """Roofline chart with matplotlib; skipped (with a message) when matplotlib is absent."""
+        """Log-log roofline: the HBM roof (bandwidth x intensity) and the tensor roof,
+        the ridge between them, and one marker per kernel at (intensity, achieved);
+        skipped with a message when matplotlib is absent."""
         try:
+            import matplotlib
+            matplotlib.use("Agg")
             import matplotlib.pyplot as plt
-            import numpy as np
         except ImportError:
             print("[profiler] matplotlib not available; skipping roofline plot")
             return
-        if not result.gpu_spec:
-            return
         g = result.gpu_spec
-        fig, ax = plt.subplots(figsize=(10, 6))
-        ax.set_xscale("log", base=2)
-        ax.set_yscale("log", base=2)
-        ai = np.logspace(-2, 10, 500, base=2)
-        ax.plot(ai, np.minimum(g.peak_bw_hbm * 1000 * ai, np.full_like(ai, g.peak_flops_fp16 * 1000)), "k-",
-                linewidth=2.5, label="Roofline (FP16 TC)")
-        for k in result.kernels:
-            if k.arithmetic_intensity > 0 and k.achieved_flops_t > 0:
-                ax.scatter(k.arithmetic_intensity, k.achieved_flops_t * 1000, s=120, zorder=5,
-                           label=f"{k.kernel_name} ({k.achieved_flops_t:.1f}T, {k.roofline_efficiency * 100:.0f}%)")
-        ax.set_xlabel("Arithmetic Intensity (FLOP/byte)")
-        ax.set_ylabel("Performance (GFLOPS)")
-        ax.set_title(f"Roofline Model — {g.name}")
-        ax.legend(loc="lower right")
-        ax.grid(True, which="both", alpha=0.3)
-        plt.tight_layout()
-        plt.savefig(output_path, dpi=150)
+        if g is None:
+            return
+        bw_gflops_per_flop_b = g.peak_bw_hbm * 1000.0          # GB/s = GFLOP/s per (FLOP/B)
+        tensor_gflops = g.peak_flops_fp16 * 1000.0
+        ridge = tensor_gflops / bw_gflops_per_flop_b
+        pts = [k for k in result.kernels if k.arithmetic_intensity > 0]
+        lo = min([ridge / 64] + [k.arithmetic_intensity / 2 for k in pts])
+        hi = max([ridge * 64] + [k.arithmetic_intensity * 2 for k in pts])
+        fig, ax = plt.subplots(figsize=(9, 5.5))
+        ax.loglog([lo, ridge], [bw_gflops_per_flop_b * lo, tensor_gflops], color="tab:blue",
+                  label=f"HBM roof {g.peak_bw_hbm * 1000:.0f} GB/s")
+        ax.loglog([ridge, hi], [tensor_gflops, tensor_gflops], color="tab:red",
+                  label=f"tensor roof {g.peak_flops_fp16:.0f} TFLOP/s")
+        ax.axvline(ridge, color="gray", linestyle=":", linewidth=1)
+        for k in pts:
+            y = k.achieved_flops_t * 1000.0 if k.achieved_flops_t > 0 else \
+                (k.hbm_read_bw_gbs + k.hbm_write_bw_gbs) * k.arithmetic_intensity
+            ax.scatter([k.arithmetic_intensity], [y], zorder=3)
+            ax.annotate(f"{k.kernel_name[:24]} {k.roofline_efficiency:.0%}", (k.arithmetic_intensity, y),
+                        textcoords="offset points", xytext=(5, -12), fontsize=8)
+        ax.set_xlabel("FLOP per DRAM byte")
+        ax.set_ylabel("GFLOP/s")
+        ax.set_title(f"{g.name}: kernels against the HBM and tensor roofs ({PEAK_SOURCE.get(g.name, 'datasheet')})")
+        ax.legend(loc="upper left")
+        fig.tight_layout()
+        fig.savefig(output_path, dpi=130)
         plt.close(fig)
-        print(f"[profiler] Roofline saved → {output_path}")
+        print(f"[profiler] roofline chart written to {output_path}")
 
 
 def ncu_available(path: str = "ncu") -> bool:
     return shutil.which(path) is not None
+
+
+def _selfcheck() -> int:
+    """Profile one 2048^3 fp16 GEMM launch through the ncu path (duration and DRAM
+    bytes only) and compare its duration with CUDA-event timing of the same call.
+    Prints one JSON line; exit status 0 when the two agree within 2x."""
+    import torch as _torch
+    from lunara_b200.runtime import ops
+    n = 2048
+    a = _torch.randn(n, n, dtype=_torch.float16, device="cuda")
+    b = _torch.randn(n, n, dtype=_torch.float16, device="cuda")
+    c = _torch.empty(n, n, dtype=_torch.float16, device="cuda")
+    flops, nbytes = 2.0 * n ** 3, 3.0 * n * n * 2
+    prof = NsightProfiler(fallback_to_events=False, launch_count=1, kernel_regex="gemm_tc", warmup=2,
+                          metrics=["gpu__time_duration.sum", "dram__bytes_read.sum", "dram__bytes_write.sum"])
+    ncu_res = prof.profile_kernel(ops.gemm, (a, b, c), {}, flops=flops, bytes_accessed=nbytes, kernel_name="gemm")
+    ev = CUDAEventProfiler(n_warmup=3, n_trials=20).profile(lambda: ops.gemm(a, b, c), flops, nbytes)
+    k = ncu_res.primary
+    out = {"ncu_kernels": len(ncu_res.kernels), "ncu_kernel": k.kernel_name if k else None,
+           "ncu_duration_us": k.duration_us if k else None, "event_duration_us": ev.duration_us,
+           "ncu_dram_read_bytes": k.raw_metrics.get("dram__bytes_read.sum") if k else None,
+           "ncu_dram_write_bytes": k.raw_metrics.get("dram__bytes_write.sum") if k else None,
+           "ratio": (k.duration_us / ev.duration_us) if k and ev.duration_us else None}
+    print(json.dumps(out))
+    if k is not None:
+        NsightProfiler.print_summary(ncu_res)
+    return 0 if out["ratio"] is not None and 0.5 <= out["ratio"] <= 2.0 else 1
+
+
+if __name__ == "__main__":
+    if "--selfcheck" in sys.argv:
+        sys.exit(_selfcheck())
+    print("usage: python -m lunara_b200.profiler.nsight_profiler --selfcheck")

@@ -56,6 +56,13 @@ SIGNATURES = {
     "lunara_version": ([], _i),
 }
 
+# Internal self-test entry points, declared in include/lunara_b200_selftest.h
+# (not part of the kernel ABI; used by the tests only).
+SELFTEST_SIGNATURES = {
+    "lunara_selftest_ex2_poly": ([_p, _p, _i64, _i, _p], _i),
+    "lunara_selftest_bounded_wait": ([ctypes.c_uint64, ctypes.c_uint, _p], _i),
+}
+
 
 class LunaraError(RuntimeError):
     """A kernel-library call returned a non-zero lunara_status."""
@@ -78,7 +85,7 @@ def load(path: os.PathLike | str | None = None) -> ctypes.CDLL:
         raise ImportError(
             f"lunara_b200 kernel library not found at {p}; build it with `python -m lunara_b200.build`")
     lib = ctypes.CDLL(str(p))
-    for name, (argtypes, restype) in SIGNATURES.items():
+    for name, (argtypes, restype) in {**SIGNATURES, **SELFTEST_SIGNATURES}.items():
         fn = getattr(lib, name)
         fn.argtypes = argtypes
         fn.restype = restype

@@ -6,12 +6,24 @@ above 1, e.g. the 4096^3 GEMM whose outputs have std 64) and relative-L2
 relative-L2 near 1e-3): max-abs <= 6e-2 (same scaling) and relative-L2 <= 5e-3.
 fp32 outputs: max-abs <= 1e-4 (scaled) and relative-L2 <= 1e-5.
 Index ops are compared bit for bit.
+
+GOLDEN_TOL: the reference's own kernel outputs (tests/golden) as the
+expected values instead of the fp32 oracle. For fp16 those outputs are
+themselves rounded to fp16 by the reference's kernel, so a comparison
+carries two output roundings (the reference's and ours) plus the
+reference's fp16 P: relative-L2 is allowed 2e-3 instead of 1e-3. fp32
+golden outputs keep the fp32 bound.
 """
 import torch
 
 TOL = {
     torch.float16: (2e-2, 1e-3),
     torch.bfloat16: (6e-2, 5e-3),
+    torch.float32: (1e-4, 1e-5),
+}
+
+GOLDEN_TOL = {
+    torch.float16: (2e-2, 2e-3),
     torch.float32: (1e-4, 1e-5),
 }
 

@@ -31,7 +31,9 @@ os.environ["TRITON_INTERPRET"] = "1"
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REF = Path(os.environ.get("LUNARA_REFERENCE", "/root/reference"))
+if "LUNARA_REFERENCE" not in os.environ:
+    sys.exit("make_golden.py: set LUNARA_REFERENCE to the reference checkout (the directory holding lunara/)")
+REF = Path(os.environ["LUNARA_REFERENCE"])
 OUT = Path(__file__).resolve().parent
 sys.path.insert(0, str(REF))
 

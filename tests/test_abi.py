@@ -3,6 +3,8 @@ points include/lunara_b200.h declares (with the signatures the ctypes binding
 assumes), and its argument validation answers before touching the device."""
 import ctypes
 import re
+import shutil
+import subprocess
 from pathlib import Path
 
 import pytest
@@ -10,11 +12,19 @@ import pytest
 from lunara_b200.runtime import _lib
 
 HEADER = Path(__file__).resolve().parents[1] / "include" / "lunara_b200.h"
+SELFTEST_HEADER = HEADER.with_name("lunara_b200_selftest.h")
 
 
-def header_functions():
-    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+def header_functions(header=HEADER):
+    text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
     return sorted(set(re.findall(r"\b(lunara_\w+)\s*\(", text)))
+
+
+def exported_functions():
+    """Every `lunara_*` function the shared library defines (dynamic symbol table)."""
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    return sorted({ln.split()[-1] for ln in out.splitlines() if ln.split()[-1].startswith("lunara_")})
 
 
 def test_library_loads_without_gpu():
@@ -29,6 +39,29 @@ def test_exports_every_declared_symbol():
     for name in declared:
         assert hasattr(lib, name), name
     assert sorted(_lib.SIGNATURES) == declared
+
+
+@pytest.mark.skipif(shutil.which("nm") is None, reason="needs nm")
+def test_export_set_equals_header_declarations():
+    """Both ways: nothing exported that no header declares, nothing declared that is not exported."""
+    declared = sorted(set(header_functions()) | set(header_functions(SELFTEST_HEADER)))
+    assert exported_functions() == declared
+    assert sorted(_lib.SELFTEST_SIGNATURES) == header_functions(SELFTEST_HEADER)
+
+
+def test_selftest_arity_matches_header():
+    text = re.sub(r"/\*.*?\*/", "", SELFTEST_HEADER.read_text(), flags=re.S)
+    for name, (argtypes, _) in _lib.SELFTEST_SIGNATURES.items():
+        m = re.search(rf"\b{name}\s*\(([^)]*)\)", text)
+        params = [p for p in m.group(1).split(",") if p.strip() and p.strip() != "void"]
+        assert len(params) == len(argtypes), name
+
+
+def test_selftest_wait_rejects_bad_arguments_on_host():
+    lib = _lib.load()
+    assert lib.lunara_selftest_bounded_wait(10, 0x401, None) == 1           # budget below 1 us
+    assert lib.lunara_selftest_bounded_wait(10 ** 10, 0x401, None) == 1     # budget above 1 s
+    assert lib.lunara_selftest_bounded_wait(10 ** 6, 0x101, None) == 1      # a product kernel's site code
 
 
 def test_signature_arity_matches_header():

@@ -204,14 +204,30 @@ def test_gemm_search_space_nonempty():
     configs = at._gemm_configs()
     assert len(configs) > 10
     for c in configs:
-        assert c.BLOCK_M == 128 and c.BLOCK_K == 64 and c.BLOCK_N in (64, 128, 192, 256)
+        assert c.BLOCK_M in (128, 256) and c.BLOCK_K == 64 and c.BLOCK_N in (64, 128, 192, 256)
         assert c.num_warps in (4, 8)
+    assert {c.BLOCK_M for c in configs} == {128, 256}          # single CTAs and CTA pairs
 
 
 def test_gemm_search_space_respects_shared_mem():
     for c in at._gemm_configs():
-        assert c.num_stages * (c.BLOCK_M + c.BLOCK_N) * c.BLOCK_K * 2 <= 227 * 1024
+        ctas = c.BLOCK_M // 128                                  # a pair splits A and B between its CTAs
+        per_cta_stage = (c.BLOCK_M + c.BLOCK_N) * c.BLOCK_K * 2 // ctas
+        assert c.num_stages * per_cta_stage + at._SMEM_RESERVED <= 227 * 1024
         assert (c.BLOCK_M + c.BLOCK_N) * c.BLOCK_K * 2 <= 96 * 1024   # the reference's per-stage rule
+
+
+def test_gemm_search_space_grid_fills_last_round():
+    # 4096^3 on 256x256 pair tiles: 256 tiles over 74 pairs = 4 rounds; 64 pairs keep 4 rounds.
+    assert at.grid_choices(4096, 4096, 256, 256) == [0, 128]
+    # out_proj 4096x768 on 128x192 tiles: 128 tiles, one round already -> full grid only.
+    assert at.grid_choices(4096, 768, 128, 192) == [0]
+    cfgs = at._gemm_configs(4096, 4096, "kn")
+    assert any(c.num_ctas == 128 and c.BLOCK_M == 256 for c in cfgs)
+    assert not any(c.BLOCK_M == 256 and c.BLOCK_N == 192 for c in cfgs)   # 192-wide pairs need [N,K] B
+    assert at.gemm_call_args(TileConfig(BLOCK_M=256, BLOCK_N=256, num_stages=5, num_ctas=128)) == \
+        dict(block_n=256, stages=5, num_ctas=128, cta_pair=2)
+    assert at.gemm_call_args(TileConfig(BLOCK_M=128, BLOCK_N=192, num_stages=4))["cta_pair"] == 1
 
 
 def test_tuning_result_hash_stable():

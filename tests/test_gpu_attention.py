@@ -14,7 +14,7 @@ import pytest
 import torch
 
 from oracle import inputs, oracle
-from tests._tol import check_close
+from tests._tol import GOLDEN_TOL, check_close
 
 pytestmark = pytest.mark.gpu
 GOLDEN = Path(__file__).resolve().parent / "golden"
@@ -103,8 +103,8 @@ def test_attention_matches_reference_golden(name):
     q, k, v, o = (torch.from_numpy(z[n]) for n in ("q", "k", "v", "o"))
     causal = name.endswith("causal")
     out = _ops().attention(q.cuda(), k.cuda(), v.cuda(), causal=causal)
-    check_close(out, o, q.dtype, name, max_abs=2e-2 if q.dtype == torch.float16 else 1e-4,
-                rel_l2=2e-3 if q.dtype == torch.float16 else 1e-5)
+    a_tol, r_tol = GOLDEN_TOL[q.dtype]
+    check_close(out, o, q.dtype, name, max_abs=a_tol, rel_l2=r_tol)
 
 
 def test_attention_deterministic_and_no_device_error():

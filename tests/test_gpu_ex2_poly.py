@@ -7,11 +7,10 @@ a running maximum that may trail the true maximum by up to 2^8, so x <= 8.
 Relative error is bounded on [-125, 8], where every result is a normal float;
 on [-126, -125] the scaled result can fall into the subnormal encoding (p(0)
 is slightly below 1), so the error there is bounded in absolute terms (these
-values are ~1e-38 and vanish in the 16-bit P anyway); below -126 the input is
-clamped and the result must stay below 2^-125.
+values are ~1e-38 and vanish in the 16-bit P anyway). Outside the range the
+result is what MUFU ex2.approx.ftz gives: exactly 0 below -126 (a masked -inf
+score contributes a zero probability, in bf16 P too) and NaN for NaN.
 """
-import ctypes
-
 import pytest
 import torch
 
@@ -21,10 +20,7 @@ pytestmark = pytest.mark.gpu
 
 
 def _run(x: torch.Tensor, pair: int) -> torch.Tensor:
-    lib = _lib.load()
-    fn = lib.lunara_selftest_ex2_poly
-    fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p]
-    fn.restype = ctypes.c_int
+    fn = _lib.load().lunara_selftest_ex2_poly
     y = torch.empty_like(x)
     rc = fn(x.data_ptr(), y.data_ptr(), x.numel(), pair, torch.cuda.current_stream().cuda_stream)
     assert rc == 0
@@ -54,7 +50,12 @@ def test_ex2_poly_pair_equals_scalar():
     assert torch.equal(_run(x, 0).view(torch.int32), _run(x, 1).view(torch.int32))
 
 
-def test_ex2_poly_clamps_underflow():
-    x = torch.tensor([-126.0, -127.5, -200.0, -1.0e30, float("-inf"), -150.25], dtype=torch.float32).cuda()
-    y = _run(x, 0).cpu()
-    assert torch.isfinite(y).all() and (y >= 0).all() and (y <= 2.0 ** -125).all(), y
+@pytest.mark.parametrize("pair", [0, 1])
+def test_ex2_poly_underflow_and_nan(pair):
+    below = torch.tensor([-126.5, -127.5, -200.0, -1.0e30, float("-inf"), -150.25], dtype=torch.float32).cuda()
+    y = _run(below, pair).cpu()
+    assert torch.equal(y, torch.zeros_like(y)), y
+    edge = _run(torch.tensor([-126.0, -126.0], dtype=torch.float32).cuda(), pair).cpu()
+    assert ((edge - 2.0 ** -126).abs() <= 2.0 ** -135).all(), edge
+    nan = _run(torch.tensor([float("nan"), 1.0], dtype=torch.float32).cuda(), pair).cpu()
+    assert torch.isnan(nan[0]) and nan[1].item() == pytest.approx(2.0, rel=1e-4), nan
