@@ -251,11 +251,11 @@ def block_kernels_cold(w, device, flush, reps: int = 16, samples: int = 5):
     """Per-launch time (ms) of each block kernel with no input in L2: a graph of
     ``reps`` launches of the kernel, each on its own block (weights and buffers),
     replayed after a 256 MB L2-flush write, timed with events around the replay."""
-    from lunara_b200.runtime.encoder import GraphRunner, KERNEL_ORDER
+    from lunara_b200.runtime.encoder import GraphRunner
     blocks = _blocks_for_cold_timing(w, reps, device)
     stream = torch.cuda.current_stream()
     out = {}
-    for name in KERNEL_ORDER:
+    for name in blocks[0].kernel_names():
         fns = [b.kernel_fns()[name] for b in blocks]
         runner = GraphRunner(lambda fns=fns: [f() for f in fns])
         times = []
@@ -277,7 +277,7 @@ def block_kernels_cold(w, device, flush, reps: int = 16, samples: int = 5):
 
 def bench_block(args, rank, world, device):
     from oracle import inputs
-    from lunara_b200.runtime.encoder import EncoderBlock, GraphRunner, KERNEL_ORDER, block_flops
+    from lunara_b200.runtime.encoder import EncoderBlock, GraphRunner, block_flops
     batch, seq = 8, 512
     x, w = inputs.block_inputs(batch, seq, seed=rank)
     blk = EncoderBlock(w, batch, seq, num_heads=12, dtype=torch.float16, device=device)
@@ -388,7 +388,7 @@ def bench_block(args, rank, world, device):
         "h2d": x_host.numel() * 2, "d2h": y_hosts[0].numel() * 2,
         "h2d_ms": h2d_ms, "d2h_ms": d2h_ms,
         "kernel_ms": kernel_ms, "dominant": dom, "flops": flops,
-        "launches_per_step": len(KERNEL_ORDER),
+        "launches_per_step": len(blk.kernel_names()),
         "clocks": clk.summary(),
         "flush": flush,
     }
@@ -426,12 +426,14 @@ def bench_stack(rank, world, device, flush, steps: int = 8, warmup: int = 3):
     runner.release()
     total = _max_over_ranks(total, world)
     ms = total / steps
+    n_kernels = len(st.blocks[0].kernel_names())
     del st
     torch.cuda.empty_cache()
     return {"layers": 12, "global_batch": 64, "seq_len": 512, "per_rank_batch": per_rank,
             "parallelism": f"batch-sharded x{world} (no collective)", "forwards": steps,
             "ms_per_forward": round(ms, 4), "tokens_per_s": 64 * 512 / (ms * 1e-3),
-            "tflops": 12 * 8 * 64.42e9 / (ms * 1e-3) / 1e12, "gpu_launches": 84 * steps}
+            "tflops": 12 * 8 * 64.42e9 / (ms * 1e-3) / 1e12,
+            "gpu_launches": 12 * n_kernels * steps}
 
 
 def tp_ffn_parity(rank, world, device):
@@ -466,6 +468,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernel-map", action="store_true",
                     help="skip the single-kernel configurations in the line's `kernels` map")
+    ap.add_argument("--no-stack", action="store_true", help="skip the 12-layer stack record")
     args = ap.parse_args()
     assert args.warmup >= 0 and args.steps >= 1
     rank, world, local = _rank_env()
@@ -494,7 +497,7 @@ def main():
 
     parity = tp_ffn_parity(rank, world, device) if world > 1 else None
     r = bench_block(args, rank, world, device)
-    stack = bench_stack(rank, world, device, r["flush"])
+    stack = None if args.no_stack else bench_stack(rank, world, device, r["flush"])
     peaks = _peaks()
     configs = None
     if rank == 0 and not args.no_kernel_map:
@@ -530,7 +533,8 @@ def main():
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, zero biases, LN 1/0)",
             "config": {**block_config(world),
                        "parallelism": f"batch-sharded replicas x{world} (no collective)",
-                       "graph": "7 kernels in one CUDA graph (programmatic dependent launch)",
+                       "graph": "5 kernels (each LayerNorm fused into the GEMM before it) in one CUDA graph "
+                                "(programmatic dependent launch)",
                        "kernel_timing": "per kernel: CUDA events around a graph of 16 launches, each on its "
                                         "own weights and buffers, after a 256 MB L2 flush; / 16, median of 5"},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": r["h2d"] * world,
@@ -548,10 +552,11 @@ def main():
                          "frac": achieved / peaks["bf16_tflops"], "traffic": traffic,
                          "timing": "cold L2 (see config.kernel_timing)",
                          "peak_source": f"{peaks['source']} bf16 burst"},
-            "stack": stack,
             "kernels": kernels,
             "clocks": r["clocks"],
         }
+        if stack is not None:
+            line["stack"] = stack
         if parity is not None:
             line["tp_ffn_parity"] = parity
         if world == 1 and not args.no_cpu_baseline:

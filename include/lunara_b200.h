@@ -93,6 +93,31 @@ int lunara_gemm(const void* A, const void* B, void* C, const void* bias, const v
                 int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int64_t ldr, int b_layout, int dtype, int activation,
                 const lunara_gemm_config* config, void* stream);
 
+/* GEMM with the post-LN residual block's LayerNorm fused into the epilogue:
+ *   Y[M,N] = LayerNorm(A[M,K] * B + bias[N] + residual[M,N]) * gamma[N] + beta[N]
+ * A, B, bias and residual as for lunara_gemm (no activation); the sum is
+ * rounded once to the output type (the value lunara_gemm would store), then
+ * normalised with fp32 statistics over exactly N columns (population
+ * variance, eps added to it). bias and residual may be NULL; Y may not alias
+ * A, B or residual. Each row's N columns are computed by one cluster of
+ * G = N / slice CTAs (slice 128, 192 or 256 columns, 2 <= G <= 8) that
+ * exchange row statistics through distributed shared memory, so no [M, N]
+ * intermediate is written. Requires f16/bf16, the TMA rules of lunara_gemm,
+ * and 16-byte aligned Y, residual, bias, gamma and beta with ldy and ldr
+ * multiples of 8; otherwise returns LUNARA_ERR_UNSUPPORTED (and launches
+ * nothing): run lunara_gemm into a buffer, then lunara_layernorm.
+ * config: block_n = slice width request, stages = ring depth, num_ctas = grid
+ * (0 = as many clusters as fit); cta_pair is ignored.
+ * Replaces: the out_proj + layernorm_attn and ffn2 + layernorm_ffn kernel
+ * pairs of the reference's block kernel list (lunara/driver.py:275-283),
+ * fused as its FusionOptions.fuse_layernorm ("fuse LayerNorm into preceding
+ * matmul", lunara/passes/operator_fusion.h:19-20) and FuseGemmEpilogue
+ * (lunara/passes/operator_fusion.cpp:71-94) intend. */
+int lunara_gemm_layernorm(const void* A, const void* B, void* Y, const void* bias, const void* residual,
+                          const void* gamma, const void* beta, int64_t M, int64_t N, int64_t K, int64_t lda,
+                          int64_t ldb, int64_t ldy, int64_t ldr, int b_layout, int dtype, float eps,
+                          const lunara_gemm_config* config, void* stream);
+
 /* Scaled-dot-product attention, O = softmax(Q K^T * scale [+ causal mask]) V.
  * Q [B,H,Sq,D], K and V [B,H,Skv,D], O [B,H,Sq,D] given by 4-entry element
  * strides (batch, head, seq, dim); the dim stride must be 1. Causal masking

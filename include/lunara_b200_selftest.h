@@ -15,9 +15,11 @@
 extern "C" {
 #endif
 
-/* y[i] = 2^x[i] over n device floats by the attention softmax's FMA-pipe
- * exponential: the scalar form (pair == 0) or the f32x2 form on pairs
- * (pair != 0, n even). Lets tests bound its error against exp2. */
+/* y[i] = 2^x[i] over n device floats by the FMA-pipe exponential: pair == 0
+ * the scalar form, 1 the f32x2 form on pairs (both with MUFU ex2's range
+ * behaviour: 0 below -126, NaN kept), 2 the clamped f32x2 form the attention
+ * softmax runs (inputs below -126 give ~2^-126); n even when pair != 0.
+ * Lets tests bound its error against exp2. */
 int lunara_selftest_ex2_poly(const float* x, float* y, int64_t n, int pair, void* stream);
 
 /* Launches one CTA that waits on an mbarrier nothing ever arrives on, with a

@@ -168,6 +168,53 @@ int lunara_gemm(const void* A, const void* B, void* C, const void* bias, const v
   return from_cuda(launch_gemm_simt(g, s), "lunara_gemm(simt)");
 }
 
+int lunara_gemm_layernorm(const void* A, const void* B, void* Y, const void* bias, const void* residual,
+                          const void* gamma, const void* beta, int64_t M, int64_t N, int64_t K, int64_t lda,
+                          int64_t ldb, int64_t ldy, int64_t ldr, int b_layout, int dtype, float eps,
+                          const lunara_gemm_config* config, void* stream) {
+  if (!valid_dtype(dtype)) return fail(LUNARA_ERR_INVALID_ARG, "lunara_gemm_layernorm: bad dtype %d", dtype);
+  if (b_layout != LUNARA_B_KN && b_layout != LUNARA_B_NK)
+    return fail(LUNARA_ERR_INVALID_ARG, "lunara_gemm_layernorm: bad b_layout %d", b_layout);
+  if (M < 0 || N <= 0 || K < 0) return fail(LUNARA_ERR_INVALID_ARG, "lunara_gemm_layernorm: bad shape");
+  if (!(eps >= 0.0f)) return fail(LUNARA_ERR_INVALID_ARG, "lunara_gemm_layernorm: eps must be >= 0");
+  if (M == 0) return ok();
+  if (!A || !B || !Y || !gamma || !beta) return fail(LUNARA_ERR_INVALID_ARG, "lunara_gemm_layernorm: NULL tensor");
+  if (lda < K || ldy < N) return fail(LUNARA_ERR_INVALID_ARG, "lunara_gemm_layernorm: lda < K or ldy < N");
+  if (b_layout == LUNARA_B_KN ? ldb < N : ldb < K)
+    return fail(LUNARA_ERR_INVALID_ARG, "lunara_gemm_layernorm: ldb too small for the B layout");
+  if (residual != nullptr && ldr < N) return fail(LUNARA_ERR_INVALID_ARG, "lunara_gemm_layernorm: ldr < N");
+  if (M >= (int64_t{1} << 31) || K < 1)
+    return fail(LUNARA_ERR_UNSUPPORTED, "lunara_gemm_layernorm: M must be below 2^31 and K positive");
+  GemmArgs g{};
+  g.A = A;
+  g.B = B;
+  g.C = Y;
+  g.bias = bias;
+  g.residual = residual;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.lda = lda;
+  g.ldb = ldb;
+  g.ldc = ldy;
+  g.ldr = ldr;
+  g.b_layout = b_layout;
+  g.dtype = dtype;
+  g.act = LUNARA_ACT_NONE;
+  if (config != nullptr) {
+    g.block_n = config->block_n;
+    g.stages = config->stages;
+    g.num_ctas = config->num_ctas;
+  }
+  if (!gemm_ln_supported(g, gamma, beta))
+    return fail(LUNARA_ERR_UNSUPPORTED,
+                "lunara_gemm_layernorm: needs f16/bf16, N = G x {128,192,256} with 2 <= G <= 8, and 16-byte "
+                "aligned operands (got N=%lld); run lunara_gemm then lunara_layernorm",
+                (long long)N);
+  return from_cuda(launch_gemm_layernorm(g, gamma, beta, eps, static_cast<cudaStream_t>(stream)),
+                   "lunara_gemm_layernorm");
+}
+
 int lunara_attention(const void* Q, const void* K, const void* V, void* O, int64_t B, int64_t H, int64_t Sq,
                      int64_t Skv, int64_t D, const int64_t* q_strides, const int64_t* k_strides,
                      const int64_t* v_strides, const int64_t* o_strides, float scale, int causal, int dtype,

@@ -62,6 +62,7 @@ constexpr float kRescaleLog2 = 8.0f;
 #define LUNARA_ATTN_POLY_PAIRS 4
 #endif
 constexpr int kPolyPairs = LUNARA_ATTN_POLY_PAIRS;
+
 static_assert(kPolyPairs >= 0 && kPolyPairs <= 16, "poly pairs per chunk");
 constexpr uint32_t kTileBytes = 128 * 128;  // one [128 x 64] 16-bit tile
 constexpr int kAttnSmem = 2 * kTileBytes + 2 * kKvStages * kTileBytes + 4 * kQTile * 4 + 512 + 1024;
@@ -392,9 +393,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_before();
       mbar_arrive(&s_free[w]);
       const int kv0 = j * kKvBlock;
-      if ((kv0 + kKvBlock > p.Skv) || (p.causal && kv0 + kKvBlock - 1 > q0)) {
+      const bool masked = (kv0 + kKvBlock > p.Skv) || (p.causal && kv0 + kKvBlock - 1 > q0);
+      int lim = kKvBlock;
+      if (masked) {
         // Keep key columns < Skv and (causal) <= this query row.
-        int lim = p.Skv - kv0;
+        lim = p.Skv - kv0;
         if (p.causal && qrow - kv0 + 1 < lim) lim = qrow - kv0 + 1;
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc)
@@ -402,7 +405,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int e = 0; e < 32; ++e)
             if (cc * 32 + e >= lim) sc[cc][e] = __float_as_uint(-INFINITY);
       }
-      // Row maximum: three-input max, eight independent partial maxima.
+      // Row maximum: three-input max, eight independent partial maxima. NaN
+      // propagates (max.NaN): a NaN score makes the running maximum, and so
+      // every exponent and the whole output row, NaN -- as the softmax of a
+      // row holding a NaN is.
       float mxp[8];
 #pragma unroll
       for (int tt = 0; tt < 8; ++tt) mxp[tt] = -INFINITY;
@@ -410,8 +416,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int cc = 0; cc < 4; ++cc)
 #pragma unroll
         for (int e = 0; e < 32; e += 2)
-          mxp[(e >> 1) & 7] = fmax3(mxp[(e >> 1) & 7], __uint_as_float(sc[cc][e]), __uint_as_float(sc[cc][e + 1]));
-      const float mx = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7]));
+          mxp[(e >> 1) & 7] = fmax3_nan(mxp[(e >> 1) & 7], __uint_as_float(sc[cc][e]), __uint_as_float(sc[cc][e + 1]));
+      const float mx = fmax3_nan(fmax3_nan(mxp[0], mxp[1], mxp[2]), fmax3_nan(mxp[3], mxp[4], mxp[5]),
+                                 fmax_nan(mxp[6], mxp[7]));
       const float m_cand = mx * sl2;
       // Running maximum: raised only when a row's maximum grows by more than
       // 2^kRescaleLog2 (decided warp-wide); O is rescaled below, once the
@@ -420,8 +427,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       float alpha = 1.f;
       if (i == 0) {
         m_used = m_cand;
-      } else if (__any_sync(0xffffffffu, m_cand > m_used + kRescaleLog2)) {
-        const float m_next = fmaxf(m_used, m_cand);
+      } else if (__any_sync(0xffffffffu, !(m_cand <= m_used + kRescaleLog2))) {   // true for NaN too
+        const float m_next = fmax_nan(m_used, m_cand);
         alpha = ex2_approx(m_used - m_next);
         l *= alpha;
         m_used = m_next;
@@ -434,23 +441,52 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint64_t negm2 = f2_pack(-m_off, -m_off);
       uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};   // packed (+0.0f, +0.0f)
       uint32_t pk[4][16];
+      // Staged in groups of 8 pairs: all scale-and-subtract FMAs of the group,
+      // then all its exponentials, then its sums and 16-bit packs, so that
+      // many independent MUFU operations are in flight at once (measured
+      // ~1% faster than one pair at a time).
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const int pair = i >> 1;
-          const bool poly = ((pair * kPolyPairs) % 16) < kPolyPairs;   // spread evenly over the chunk
-          const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sc[c][i]), __uint_as_float(sc[c][i + 1])), sl2x2, negm2);
-          uint64_t e2;
-          if (poly) {
-            e2 = ex2_poly2(x2);
-          } else {
-            const float2 x = f2_unpack(x2);
-            e2 = f2_pack(ex2_approx(x.x), ex2_approx(x.y));
+        for (int g0 = 0; g0 < 16; g0 += 8) {
+          uint64_t x2[8], e2[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int i = 2 * (g0 + q);
+            x2[q] = f2_fma(f2_pack(__uint_as_float(sc[c][i]), __uint_as_float(sc[c][i + 1])), sl2x2, negm2);
           }
-          sum2[pair & 3] = f2_add(sum2[pair & 3], e2);
-          const float2 e = f2_unpack(e2);
-          pk[c][pair] = Io<T>::pack2(e.x, e.y);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int pair = g0 + q;
+            if (((pair * kPolyPairs) % 16) < kPolyPairs) {   // spread evenly over the chunk
+              e2[q] = ex2_poly2_clamped(x2[q]);
+            } else {
+              const float2 x = f2_unpack(x2[q]);
+              e2[q] = f2_pack(ex2_approx(x.x), ex2_approx(x.y));
+            }
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int pair = g0 + q;
+            sum2[pair & 3] = f2_add(sum2[pair & 3], e2[q]);
+            const float2 e = f2_unpack(e2[q]);
+            pk[c][pair] = Io<T>::pack2(e.x, e.y);
+          }
+        }
+      }
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        // The FMA-pipe exponential gives ~2^-126 for a masked (-inf) score,
+        // which bf16 can hold: masked columns get an exact zero P here (the
+        // fp16 rounding already flushes it to zero).
+        if (masked) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int pair = 0; pair < 16; ++pair) {
+              const int col = c * 32 + 2 * pair;
+              if (col >= lim) pk[c][pair] = 0u;
+              else if (col + 1 >= lim) pk[c][pair] &= 0xFFFFu;
+            }
         }
       }
       const float2 ls = f2_unpack(f2_add(f2_add(sum2[0], sum2[1]), f2_add(sum2[2], sum2[3])));
@@ -506,7 +542,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const float m0 = s_stats[0 * kQTile + r], l0 = s_stats[1 * kQTile + r];
       const float m1 = s_stats[2 * kQTile + r], l1 = s_stats[3 * kQTile + r];
       const bool has0 = nb_h0 > 0, has1 = nb_h1 > 0;
-      const float m = fmaxf(has0 ? m0 : -INFINITY, has1 ? m1 : -INFINITY);
+      const float m = fmax_nan(has0 ? m0 : -INFINITY, has1 ? m1 : -INFINITY);
       const float a0 = (has0 && m0 != -INFINITY) ? ex2_approx(m0 - m) : 0.f;
       const float a1 = (has1 && m1 != -INFINITY) ? ex2_approx(m1 - m) : 0.f;
       const float inv_l = 1.0f / (l0 * a0 + l1 * a1);

@@ -371,14 +371,21 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t local_addr, uint32_t ra
   return r;
 }
 
-// Asynchronous 8-byte store into (possibly another CTA's) shared memory that
-// completes 8 transaction bytes on the mbarrier at `remote_bar` in the same
-// CTA as the destination.
-__device__ __forceinline__ void st_async_v2_f32(uint32_t remote_addr, float a, float b, uint32_t remote_bar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
-                   remote_addr),
-               "f"(a), "f"(b), "r"(remote_bar)
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
+// from this CTA's shared memory into shared memory of a CTA of the cluster,
+// completing that many transaction bytes on the mbarrier at `dst_bar` (in the
+// destination CTA).
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster_addr, uint32_t src_addr, uint32_t bytes,
+                                                     uint32_t dst_bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst_cluster_addr),
+               "r"(src_addr), "r"(bytes), "r"(dst_bar)
                : "memory");
+}
+
+// Raise the pending transaction count of the current phase without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
 // try_wait whose acquire covers writes made by other CTAs of the cluster.
@@ -555,8 +562,14 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
-// ex2_poly for a pair, with the additions and the cubic on the f32x2 pipe.
-__device__ __forceinline__ uint64_t ex2_poly2(uint64_t x2) {
+// ex2_poly for a pair, with the additions and the cubic on the f32x2 pipe,
+// without the range correction: exact to the cubic's error for x >= -126;
+// below that (and for NaN) the input is clamped to -126, so the result is
+// ~2^-126, not 0. The attention softmax uses this form in its inner loop: its
+// row maximum propagates NaN (a NaN score makes the whole row NaN through the
+// MUFU columns) and it zeroes masked columns itself where 2^-126 would
+// survive the rounding to the 16-bit P (bf16).
+__device__ __forceinline__ uint64_t ex2_poly2_clamped(uint64_t x2) {
   float2 x = f2_unpack(x2);
   const uint64_t xc = f2_pack(fmaxf(x.x, -126.0f), fmaxf(x.y, -126.0f));
   const uint64_t t = f2_add(xc, f2_pack(12582912.0f, 12582912.0f));
@@ -566,8 +579,28 @@ __device__ __forceinline__ uint64_t ex2_poly2(uint64_t x2) {
   p = f2_fma(p, f, f2_pack(0.9999280572f, 0.9999280572f));
   const float2 tv = f2_unpack(t), pv = f2_unpack(p);
   // (bits(t) - bits(1.5 * 2^23)) << 23 == bits(t) << 23 modulo 2^32.
-  return f2_pack(ex2_fix_range(x.x, __uint_as_float(__float_as_uint(pv.x) + (__float_as_uint(tv.x) << 23))),
-                 ex2_fix_range(x.y, __uint_as_float(__float_as_uint(pv.y) + (__float_as_uint(tv.y) << 23))));
+  return f2_pack(__uint_as_float(__float_as_uint(pv.x) + (__float_as_uint(tv.x) << 23)),
+                 __uint_as_float(__float_as_uint(pv.y) + (__float_as_uint(tv.y) << 23)));
+}
+
+// ex2_poly for a pair with MUFU's range behaviour (0 below -126, NaN kept).
+__device__ __forceinline__ uint64_t ex2_poly2(uint64_t x2) {
+  const float2 x = f2_unpack(x2);
+  const float2 r = f2_unpack(ex2_poly2_clamped(x2));
+  return f2_pack(ex2_fix_range(x.x, r.x), ex2_fix_range(x.y, r.y));
+}
+
+// max(a, b) and max(a, b, c) that return NaN when any input is NaN.
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+__device__ __forceinline__ float fmax3_nan(float a, float b, float c) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 __device__ __forceinline__ float tanh_approx(float x) {

@@ -983,6 +983,425 @@ cudaError_t dispatch_plan(const GemmArgs& g, GemmPlan plan, cudaStream_t s) {
   }
 }
 
+
+// ------------------------------------------- GEMM + residual + LayerNorm ----
+// Y = LayerNorm(A * B + bias + residual) * gamma + beta over rows of N = G * BN
+// columns, each row split over a cluster of G CTAs (2 <= G <= 8): CTA r of a
+// cluster computes columns [r * BN, (r + 1) * BN) of the same 128 rows with the
+// single-CTA main loop above (TMA warp, MMA thread, two TMEM accumulators), and
+// the cluster loops persistently over 128-row blocks. The epilogue warps
+//   1. read their 32-column chunks from TMEM, add bias and residual in fp32
+//      and round once to the output type -- the value the unfused GEMM would
+//      store for the LayerNorm to read -- keeping the rounded row segment
+//      packed in registers, then hand the accumulator back;
+//   2. take the mean and M2 (sum of squared deviations) of their row segment
+//      (exact two-pass over the registers), write that pair into the row's
+//      slot of the CTA's statistics buffer, and send the warp's 32 pairs
+//      (256 bytes) to the same slot of every other CTA of the cluster with one
+//      bulk copy each, which completes its bytes on the receiving CTA's
+//      statistics barrier (36 barrier updates per CTA for G = 4, where one
+//      8-byte store per row and CTA took 1536 and cost as much as a
+//      separate LayerNorm kernel);
+//   3. once all 3 * G pairs of the block have arrived, combine them (Chan et
+//      al.'s pairwise update with known counts) into the row's mean and
+//      population variance over N, normalise, scale by gamma, add beta, round
+//      once and write the output chunk with a TMA store.
+// No intermediate [M, N] tensor is written or read back. Statistics buffers
+// alternate with the block parity: a CTA can send block t+2's pairs only after
+// every CTA of the cluster has sent its block t+1 pairs, which each warp does
+// only after reading its block t pairs, so a buffer is never overwritten while
+// it is read. Every CTA of a cluster passes a final cluster barrier before it
+// exits, so no st.async can target the shared memory of a CTA that has left.
+struct LnParams {
+  const void* gamma;
+  const void* beta;
+  float eps;
+};
+
+__host__ __device__ constexpr int ln_reserve(int G) {
+  return 1024 + kEpiWarps * kStageC + 2 * 3 * G * BM * 8 + 512 + kEpiWarps * 3 * kBiasPerWarp * 4;
+}
+
+constexpr int ln_stage_bytes(int bn) { return BM * BK * 2 + bn * BK * 2; }
+
+constexpr int ln_max_stages(int bn, int G) {
+  return std::min(8, (kMaxDynSmem - ln_reserve(G)) / ln_stage_bytes(bn));
+}
+
+template <typename T, int BN, bool B_KMAJOR>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_ln_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                   const __grid_constant__ CUtensorMap tma_c, const EpiParams ep, const LnParams ln, const int M,
+                   const int K, const int STAGES, unsigned int* err) {
+  constexpr uint32_t A_BYTES = BM * BK * 2;
+  constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr uint32_t TMEM_COLS = tmem_cols_for(BN);
+  constexpr uint32_t ACC_STRIDE = TMEM_COLS / 2;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t IDESC = idesc_f16(BM, BN, kBF16, false, !B_KMAJOR);
+  constexpr int kChunks = BN / 32;
+  constexpr int kWarpChunks = (kChunks + kEpiSlices - 1) / kEpiSlices;   // most chunks one warp owns
+  static_assert(kChunks >= kEpiSlices && kWarpChunks <= kMaxWarpChunks, "every epilogue warp owns a chunk");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t{1023});
+  const uint32_t G = cluster_nctarank();
+  const uint32_t rank = cluster_ctarank();
+  const int nslots = 3 * static_cast<int>(G);
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * A_BYTES;
+  uint8_t* sC = sB + STAGES * B_BYTES;                                       // kEpiWarps x kStageC
+  float2* s_stats = reinterpret_cast<float2*>(sC + kEpiWarps * kStageC);    // [2][nslots][BM] (mean, M2)
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(s_stats + 2 * nslots * BM);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint64_t* stats_bar = drain_bar + 1;                                      // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(stats_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_vec = reinterpret_cast<float*>(stats_bar + 4);   // [kEpiWarps][bias | gamma | beta][kBiasPerWarp]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int cid = static_cast<int>(cluster_id_x());
+  const int ncl = static_cast<int>(nclusters_x());
+  const int m_tiles = (M + BM - 1) / BM;
+  const int kblocks = (K + BK - 1) / BK;
+  const int n0 = static_cast<int>(rank) * BN;
+  const int N = static_cast<int>(G) * BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], kEpiWarps);
+      mbar_init(&stats_bar[a], kEpiThreads);   // every epilogue thread, after writing its local pair
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  cluster_sync();   // every CTA's statistics barriers are initialised before any st.async targets them
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  if (warp == 0 && lane == 0 && cid < m_tiles) {
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+    for (int kb = 0; kb < kblocks && kb < STAGES; ++kb) {
+      if constexpr (B_KMAJOR) {
+        tma_prefetch_l2_2d(&tma_b, kb * BK, n0);
+      } else {
+#pragma unroll
+        for (int j = 0; j < BN / 64; ++j) tma_prefetch_l2_2d(&tma_b, n0 + j * 64, kb * BK);
+      }
+    }
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------ TMA producer --
+      uint32_t stage = 0, phase = 0, issued = 0;
+      bool ok = true;
+      for (int tile = cid; ok && tile < m_tiles; tile += ncl) {
+        const int m0 = tile * BM;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, err, kErrGemmProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[stage], A_BYTES + B_BYTES);
+          tma_load_2d(sA + stage * A_BYTES, &tma_a, &full_bar[stage], kb * BK, m0);
+          if constexpr (B_KMAJOR) {
+            tma_load_2d(sB + stage * B_BYTES, &tma_b, &full_bar[stage], kb * BK, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sB + stage * B_BYTES + j * (BK * 128), &tma_b, &full_bar[stage], n0 + j * 64, kb * BK);
+          }
+          ++issued;
+          if (++stage == static_cast<uint32_t>(STAGES)) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        const uint32_t first = issued > static_cast<uint32_t>(STAGES) ? issued - STAGES : 0u;
+        for (uint32_t i = first; i < issued; ++i)
+          mbar_drain_wait(&full_bar[i % STAGES], (i / STAGES) & 1u, 1000000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------- MMA issuer --
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = cid; ok && tile < m_tiles; tile += ncl) {
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, err, kErrGemmMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * ACC_STRIDE;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, err, kErrGemmMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = sw128_desc(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = B_KMAJOR ? sw128_desc(b_addr + k * 32, 16, 1024)
+                                         : sw128_desc(b_addr + k * 2048, BK * 128, 1024);
+            umma_f16_ss(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == static_cast<uint32_t>(STAGES)) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        umma_commit(drain_bar);
+        mbar_drain_wait(drain_bar, 0, 1000000000ull);
+      }
+    }
+  } else {
+    // ----------------------------------------------------------- epilogue --
+    // Warps 2..13: warp & 3 is the TMEM lane quarter (rows 32q .. 32q+31 of the
+    // block), (warp - 2) / 4 the column slice: chunks slice, slice + 3, ...
+    const int quarter = warp & 3;
+    const int slice = (warp - 2) >> 2;
+    const int row_t = quarter * 32 + lane;
+    float* sv = s_vec + (warp - 2) * 3 * kBiasPerWarp;
+    uint8_t* s_stage = sC + (warp - 2) * kStageC;
+    // Bias, gamma and beta of this warp's columns: the same for every block.
+#pragma unroll
+    for (int j = 0; j < kWarpChunks; ++j) {
+      const int c = slice + j * kEpiSlices;
+      if (c >= kChunks) break;
+      const int col = n0 + c * 32 + lane;
+      sv[j * 32 + lane] = ep.bias != nullptr ? Io<T>::to_f(static_cast<const T*>(ep.bias)[col]) : 0.f;
+      sv[kBiasPerWarp + j * 32 + lane] = Io<T>::to_f(static_cast<const T*>(ln.gamma)[col]);
+      sv[2 * kBiasPerWarp + j * 32 + lane] = Io<T>::to_f(static_cast<const T*>(ln.beta)[col]);
+    }
+    __syncwarp();
+    const int my_chunks = (kChunks - slice + kEpiSlices - 1) / kEpiSlices;
+    const float inv_mine = 1.0f / static_cast<float>(my_chunks * 32);
+    const float inv_n = 1.0f / static_cast<float>(N);
+    uint32_t acc = 0, acc_phase = 0;
+    int it = 0;
+    for (int tile = cid; tile < m_tiles; tile += ncl, ++it) {
+      const int m0 = tile * BM;
+      const int row = m0 + row_t;
+      ResChunk res;
+      load_residual<T>(res, row, n0 + slice * 32, ep);
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, err, kErrGemmEpilogue)) break;
+      tc_fence_after();
+      const uint32_t t_tile = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * ACC_STRIDE;
+      // 1. acc + bias + residual, rounded once, packed in registers.
+      uint32_t pk[kWarpChunks][16];
+      float sum0 = 0.f, sum1 = 0.f;
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(t_tile + slice * 32, v);
+#pragma unroll
+      for (int j = 0; j < kWarpChunks; ++j) {
+        const int c = slice + j * kEpiSlices;
+        if (c >= kChunks) break;
+        tmem_ld_wait_regs(v);
+        epilogue_pack<T, kEpiPlain>(v, row, n0 + c * 32, sv + j * 32, res, ep, pk[j]);
+        if (c + kEpiSlices < kChunks) {
+          tmem_ld_32x32b_x32(t_tile + (c + kEpiSlices) * 32, v);
+          load_residual<T>(res, row, n0 + (c + kEpiSlices) * 32, ep);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 f = Io<T>::unpack2(pk[j][i]);
+          sum0 += f.x;
+          sum1 += f.y;
+        }
+      }
+      // The accumulator is in registers: hand the TMEM buffer back to the MMA thread.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+      // 2. This segment's mean and M2, sent to slot (rank, slice) of every CTA.
+      const float mean_l = (sum0 + sum1) * inv_mine;
+      float m2v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < kWarpChunks; ++j) {
+        if (slice + j * kEpiSlices >= kChunks) break;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 f = Io<T>::unpack2(pk[j][i]);
+          const float da = f.x - mean_l, db = f.y - mean_l;
+          m2v[(2 * i) & 3] = fmaf(da, da, m2v[(2 * i) & 3]);
+          m2v[(2 * i + 1) & 3] = fmaf(db, db, m2v[(2 * i + 1) & 3]);
+        }
+      }
+      const int b = it & 1;
+      const uint32_t bphase = static_cast<uint32_t>(it >> 1) & 1u;
+      float2* seg = &s_stats[(b * nslots + static_cast<int>(rank) * kEpiSlices + slice) * BM + quarter * 32];
+      seg[lane] = make_float2(mean_l, (m2v[0] + m2v[1]) + (m2v[2] + m2v[3]));
+      fence_proxy_async_smem();   // the pairs are visible to the bulk copies below
+      __syncwarp();
+      if (warp == 2 && lane == 0)
+        mbar_expect_tx(&stats_bar[b], (G - 1u) * static_cast<uint32_t>(kEpiWarps * 32 * 8));
+      mbar_arrive(&stats_bar[b]);
+      if (lane == 0) {
+        const uint32_t src = smem_u32(seg);
+        const uint32_t bar_addr = smem_u32(&stats_bar[b]);
+        for (uint32_t r = 0; r < G; ++r)
+          if (r != rank) bulk_copy_to_cluster(mapa_shared(src, r), src, 32 * 8, mapa_shared(bar_addr, r));
+      }
+      if (!mbar_wait_cluster(&stats_bar[b], bphase, abort_flag, err, kErrGemmEpilogue)) break;
+      // 3. Row statistics over all N columns, then normalise and store.
+      const float2* st = s_stats + b * nslots * BM + row_t;
+      float wsum = 0.f;
+      for (int sl = 0; sl < nslots; ++sl) {
+        const int cnt = 32 * ((kChunks - (sl % kEpiSlices) + kEpiSlices - 1) / kEpiSlices);
+        wsum = fmaf(static_cast<float>(cnt), st[sl * BM].x, wsum);
+      }
+      const float mean = wsum * inv_n;
+      float m2 = 0.f;
+      for (int sl = 0; sl < nslots; ++sl) {
+        const int cnt = 32 * ((kChunks - (sl % kEpiSlices) + kEpiSlices - 1) / kEpiSlices);
+        const float2 pr = st[sl * BM];
+        const float d = pr.x - mean;
+        m2 += pr.y + static_cast<float>(cnt) * d * d;
+      }
+      const float rstd = rsqrtf(m2 * inv_n + ln.eps);
+#pragma unroll
+      for (int j = 0; j < kWarpChunks; ++j) {
+        const int c = slice + j * kEpiSlices;
+        if (c >= kChunks) break;
+        const float* g = sv + kBiasPerWarp + j * 32;
+        const float* be = sv + 2 * kBiasPerWarp + j * 32;
+        uint32_t out[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 f = Io<T>::unpack2(pk[j][i]);
+          out[i] = Io<T>::pack2(fmaf((f.x - mean) * rstd, g[2 * i], be[2 * i]),
+                                fmaf((f.y - mean) * rstd, g[2 * i + 1], be[2 * i + 1]));
+        }
+        store_chunk_tma(out, n0 + c * 32, m0 + quarter * 32, &tma_c, s_stage, lane);
+      }
+    }
+    if (lane == 0) bulk_wait_group_all();   // output stores done before the CTA exits
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+  cluster_sync();   // no CTA leaves while a peer may still send statistics into its shared memory
+}
+
+template <typename T, int BN, bool B_KMAJOR>
+cudaError_t run_ln(const GemmArgs& g, const LnParams& ln, int G, const CUtensorMap& ma, const CUtensorMap& mb,
+                   const CUtensorMap& mc, const EpiParams& ep, cudaStream_t s) {
+  auto kern = gemm_ln_kernel<T, BN, B_KMAJOR>;
+  const int max_stages = ln_max_stages(BN, G);
+  if (max_stages < 2) return cudaErrorInvalidConfiguration;
+  const int stages = (g.stages >= 2 && g.stages <= max_stages) ? g.stages : std::min(4, max_stages);
+  const int smem = stages * ln_stage_bytes(BN) + ln_reserve(G);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+  if (e != cudaSuccess) return e;
+  // Persistent grid: as many clusters of G as can be resident, cached per
+  // (device, G, stages) under a lock; never more clusters than row blocks.
+  static std::mutex cache_mu;
+  static int cached[64][9][9] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+  const bool cacheable = dev >= 0 && dev < 64;
+  int max_clusters = 0;
+  if (cacheable) {
+    std::lock_guard<std::mutex> lk(cache_mu);
+    max_clusters = cached[dev][G][stages];
+  }
+  if (max_clusters == 0) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(G);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(G * (device_num_sms() / G)));
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      return cudaErrorInvalidConfiguration;
+    }
+    max_clusters = n;
+    if (cacheable) {
+      std::lock_guard<std::mutex> lk(cache_mu);
+      cached[dev][G][stages] = max_clusters;
+    }
+  }
+  const int64_t m_tiles = ceil_div64(g.M, BM);
+  int64_t clusters = g.num_ctas >= G ? g.num_ctas / G : max_clusters;
+  if (clusters > max_clusters) clusters = max_clusters;
+  if (clusters > m_tiles) clusters = m_tiles;
+  if (clusters < 1) clusters = 1;
+  unsigned int* err = device_error_word();
+  if (err == nullptr) return cudaErrorInvalidDevice;
+  return launch_pdl_cluster(kern, dim3(static_cast<unsigned>(clusters * G)), dim3(kGemmThreads),
+                            static_cast<unsigned>(G), static_cast<size_t>(smem), s, ma, mb, mc, ep, ln,
+                            static_cast<int>(g.M), static_cast<int>(g.K), stages, err);
+}
+
+template <typename T, bool B_KMAJOR>
+cudaError_t dispatch_ln(const GemmArgs& g, const LnParams& ln, int bn, cudaStream_t s) {
+  const int G = static_cast<int>(g.N / bn);
+  CUtensorMap ma, mb, mc;
+  if (!encode_2d(&ma, g.A, g.dtype, g.K, g.M, g.lda * 2, BK, BM)) return cudaErrorInvalidValue;
+  const bool ok_b = B_KMAJOR ? encode_2d(&mb, g.B, g.dtype, g.K, g.N, g.ldb * 2, BK, bn)
+                             : encode_2d(&mb, g.B, g.dtype, g.N, g.K, g.ldb * 2, 64, BK);
+  if (!ok_b) return cudaErrorInvalidValue;
+  EpiParams ep = make_epi(g);
+  if (!encode_2d(&mc, g.C, g.dtype, g.N, g.M, g.ldc * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+    return cudaErrorInvalidValue;
+  ep.tma_store = 1;
+  switch (bn) {
+    case 128: return run_ln<T, 128, B_KMAJOR>(g, ln, G, ma, mb, mc, ep, s);
+    case 192: return run_ln<T, 192, B_KMAJOR>(g, ln, G, ma, mb, mc, ep, s);
+    default: return run_ln<T, 256, B_KMAJOR>(g, ln, G, ma, mb, mc, ep, s);
+  }
+}
+
 }  // namespace
 
 bool gemm_tc_supported(const GemmArgs& g) {
@@ -1030,6 +1449,43 @@ cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t stream) {
       break;
   }
   return cudaGetLastError();
+}
+
+}  // namespace lunara
+
+namespace lunara {
+
+int gemm_ln_block_n(int64_t N, int requested) {
+  // Column slice per CTA: the requested one when it divides N into 2..8 slices,
+  // else 192, 256, 128 in that order of preference (192 gives the 4-CTA
+  // clusters that cover 768 columns with one 128 x 192 tile per CTA).
+  const int pref[4] = {requested, 192, 256, 128};
+  for (int bn : pref) {
+    if (bn != 128 && bn != 192 && bn != 256) continue;
+    if (N % bn == 0 && N / bn >= 2 && N / bn <= 8) return bn;
+  }
+  return 0;
+}
+
+bool gemm_ln_supported(const GemmArgs& g, const void* gamma, const void* beta) {
+  if (g.dtype != LUNARA_F16 && g.dtype != LUNARA_BF16) return false;
+  if (g.act != LUNARA_ACT_NONE) return false;
+  if (!gemm_tc_supported(g)) return false;
+  if (gemm_ln_block_n(g.N, g.block_n) == 0) return false;
+  const EpiParams ep = make_epi(g);
+  if (!ep.vec_ok) return false;
+  return al16(gamma) && al16(beta);
+}
+
+cudaError_t launch_gemm_layernorm(const GemmArgs& g, const void* gamma, const void* beta, float eps,
+                                  cudaStream_t stream) {
+  LnParams ln{gamma, beta, eps};
+  const int bn = gemm_ln_block_n(g.N, g.block_n);
+  const bool kmajor = g.b_layout == LUNARA_B_NK;
+  if (g.dtype == LUNARA_BF16)
+    return kmajor ? dispatch_ln<__nv_bfloat16, true>(g, ln, bn, stream)
+                  : dispatch_ln<__nv_bfloat16, false>(g, ln, bn, stream);
+  return kmajor ? dispatch_ln<__half, true>(g, ln, bn, stream) : dispatch_ln<__half, false>(g, ln, bn, stream);
 }
 
 }  // namespace lunara

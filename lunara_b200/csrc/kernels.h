@@ -31,6 +31,27 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
+// As launch_pdl, for a kernel launched in clusters of `cluster` CTAs along x.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, unsigned cluster, size_t smem,
+                               cudaStream_t s, Args&&... args) {
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // Device address of the library's error word on the current device (cached
 // per device); nullptr when the symbol cannot be resolved.
 unsigned int* device_error_word();
@@ -76,6 +97,14 @@ struct GemmArgs {
 // True when the tcgen05/TMA path accepts the shapes, strides and pointers.
 bool gemm_tc_supported(const GemmArgs& g);
 cudaError_t launch_gemm_tcgen05(const GemmArgs& g, cudaStream_t stream);
+
+// GEMM + bias + residual + LayerNorm over the N columns of each row, N split
+// over a cluster of 2..8 CTAs (N = G * block_n, block_n 128 / 192 / 256).
+// gemm_ln_block_n returns the slice width for N (0 when none fits).
+int gemm_ln_block_n(int64_t N, int requested);
+bool gemm_ln_supported(const GemmArgs& g, const void* gamma, const void* beta);
+cudaError_t launch_gemm_layernorm(const GemmArgs& g, const void* gamma, const void* beta, float eps,
+                                  cudaStream_t stream);
 cudaError_t launch_gemm_simt(const GemmArgs& g, cudaStream_t stream);
 
 struct AttnArgs {

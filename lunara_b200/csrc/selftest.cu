@@ -13,12 +13,15 @@
 namespace lunara {
 namespace {
 
-// y[i] = 2^x[i]: the scalar ex2_poly (pair == 0) or the f32x2 ex2_poly2 on (x[2i], x[2i+1]).
-__global__ void ex2_poly_selftest_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n, int pair) {
+// y[i] = 2^x[i]: the scalar ex2_poly (mode 0), the f32x2 ex2_poly2 on
+// (x[2i], x[2i+1]) (mode 1), or the clamped f32x2 form the attention softmax
+// runs, ex2_poly2_clamped (mode 2).
+__global__ void ex2_poly_selftest_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n, int mode) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (pair) {
+  if (mode) {
     if (2 * i + 1 >= n) return;
-    const float2 r = f2_unpack(ex2_poly2(f2_pack(x[2 * i], x[2 * i + 1])));
+    const uint64_t in = f2_pack(x[2 * i], x[2 * i + 1]);
+    const float2 r = f2_unpack(mode == 2 ? ex2_poly2_clamped(in) : ex2_poly2(in));
     y[2 * i] = r.x;
     y[2 * i + 1] = r.y;
   } else if (i < n) {
@@ -51,6 +54,7 @@ __global__ void bounded_wait_selftest_kernel(unsigned long long budget_ns, unsig
 extern "C" {
 
 int lunara_selftest_ex2_poly(const float* x, float* y, int64_t n, int pair, void* stream) {
+  if (pair < 0 || pair > 2) return 1;
   if (n < 0 || (n > 0 && (x == nullptr || y == nullptr)) || (pair && (n & 1)) || n > (int64_t{1} << 30)) return 1;
   if (n == 0) return 0;
   const int64_t threads = pair ? n / 2 : n;

@@ -39,6 +39,8 @@ class GemmConfig(ctypes.Structure):
 SIGNATURES = {
     "lunara_gemm": ([_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _i, _i,
                      ctypes.POINTER(GemmConfig), _p], _i),
+    "lunara_gemm_layernorm": ([_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _i, _f,
+                               ctypes.POINTER(GemmConfig), _p], _i),
     "lunara_attention": ([_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64, _pi64, _pi64,
                           _f, _i, _i, _p], _i),
     "lunara_layernorm": ([_p, _p, _p, _p, _i64, _i64, _f, _i, _p], _i),

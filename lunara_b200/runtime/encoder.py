@@ -4,16 +4,21 @@ Runs the kernel set of one post-LN transformer encoder block -- the seven
 kernels of lunara/driver.py:275-283 (qkv_proj, flash_attn, out_proj,
 layernorm_attn, ffn1, ffn2, layernorm_ffn) -- on device-resident weights and
 activation buffers, optionally captured once into a CUDA graph and replayed.
+By default each LayerNorm is fused into the GEMM before it
+(lunara_gemm_layernorm, the reference's FusionOptions.fuse_layernorm,
+lunara/passes/operator_fusion.h:19-20), so the block runs five kernels:
+qkv_proj, flash_attn, out_proj+layernorm_attn, ffn1, ffn2+layernorm_ffn.
 
 Data layout in HBM (tokens T = B*S, hidden Hd, heads H, head dim D = Hd/H):
   x      [T, Hd]            input / residual of the attention sub-layer
   qkv    [T, 3*Hd]          = [B, S, 3, H, D]; attention reads Q, K and V from
                             it in place through 4-D tensor maps (no split copy)
   attn   [T, Hd]            attention output written as [B, S, H, D]
-  h      [T, Hd]            out_proj + bias + residual(x)   (fused epilogue)
+  h      [T, Hd]            out_proj + bias + residual(x)   (fused epilogue; unused when
+                            the LayerNorm is fused as well)
   x1     [T, Hd]            LayerNorm(h)
   f      [T, F]             GELU(x1 W1^T + b1)               (fused epilogue)
-  g      [T, Hd]            f W2^T + b2 + residual(x1)       (fused epilogue)
+  g      [T, Hd]            f W2^T + b2 + residual(x1)       (unused when fused)
   y      [T, Hd]            LayerNorm(g)
 Linear weights are kept as [out, in] (K-major for the tcgen05 B operand).
 """
@@ -31,13 +36,15 @@ WEIGHT_NAMES = ("w_qkv", "b_qkv", "w_o", "b_o", "ln1_w", "ln1_b", "w_1", "b_1", 
 
 # Kernel names in execution order, as in the reference's block spec list.
 KERNEL_ORDER = ("qkv_proj", "flash_attn", "out_proj", "layernorm_attn", "ffn1", "ffn2", "layernorm_ffn")
+# The same block with each LayerNorm fused into the GEMM before it.
+FUSED_KERNEL_ORDER = ("qkv_proj", "flash_attn", "out_proj+layernorm_attn", "ffn1", "ffn2+layernorm_ffn")
 
 
 def block_flops(tokens: int, seq: int, hidden: int = 768, heads: int = 12, ffn: int = 3072) -> Dict[str, float]:
     """Algorithmic FLOPs per kernel of one block (2MNK per GEMM, 4*B*H*S^2*D attention)."""
     batch = tokens // seq
     d = hidden // heads
-    return {
+    f = {
         "qkv_proj": 2.0 * tokens * hidden * 3 * hidden,
         "flash_attn": 4.0 * batch * heads * seq * seq * d,
         "out_proj": 2.0 * tokens * hidden * hidden,
@@ -46,6 +53,9 @@ def block_flops(tokens: int, seq: int, hidden: int = 768, heads: int = 12, ffn: 
         "ffn2": 2.0 * tokens * ffn * hidden,
         "layernorm_ffn": 0.0,
     }
+    f["out_proj+layernorm_attn"] = f["out_proj"]
+    f["ffn2+layernorm_ffn"] = f["ffn2"]
+    return f
 
 
 class EncoderBlock:
@@ -54,9 +64,10 @@ class EncoderBlock:
     def __init__(self, weights: Dict[str, torch.Tensor], batch: int, seq: int, num_heads: int = 12,
                  dtype: torch.dtype = torch.float16, device: Optional[torch.device] = None,
                  eps: float = 1e-5, ffn_activation: str = "gelu_tanh",
-                 gemm_tiles: Optional[Dict[str, Dict[str, int]]] = None):
+                 gemm_tiles: Optional[Dict[str, Dict[str, int]]] = None, fuse_layernorm: bool = True):
         device = torch.device(device or "cuda")
         self.batch, self.seq, self.heads, self.dtype, self.eps = batch, seq, num_heads, dtype, eps
+        self.fuse_layernorm = fuse_layernorm
         self.ffn_activation = ffn_activation
         self.gemm_tiles = gemm_tiles or {}
         self.w = {k: weights[k].to(device=device, dtype=dtype).contiguous() for k in WEIGHT_NAMES}
@@ -85,16 +96,34 @@ class EncoderBlock:
     def _tile(self, name: str) -> Dict[str, int]:
         return self.gemm_tiles.get(name, {})
 
+    def kernel_names(self):
+        return FUSED_KERNEL_ORDER if self.fuse_layernorm else KERNEL_ORDER
+
     def kernel_fns(self, x: Optional[torch.Tensor] = None,
                    out: Optional[torch.Tensor] = None) -> "OrderedDict[str, Callable[[], object]]":
-        """The seven launches of one block forward (x, default self.x -> out, default self.y),
-        in order, keyed by the names of KERNEL_ORDER."""
+        """The launches of one block forward (x, default self.x -> out, default self.y), in
+        order, keyed by the names of FUSED_KERNEL_ORDER (LayerNorm fused, the default) or
+        KERNEL_ORDER."""
         x = self.x if x is None else x
         y = self.y if out is None else out
         w = self.w
         B, S, H, D = self.batch, self.seq, self.heads, self.head_dim
         q, k, v = self._qkv_views()
         o = self.attn.view(B, S, H, D).permute(0, 2, 1, 3)
+        if self.fuse_layernorm:
+            return OrderedDict([
+                ("qkv_proj", lambda: ops.gemm(x, w["w_qkv"], self.qkv, bias=w["b_qkv"], b_layout="nk",
+                                              **self._tile("qkv_proj"))),
+                ("flash_attn", lambda: ops.attention(q, k, v, causal=False, scale=self.scale, out=o)),
+                ("out_proj+layernorm_attn",
+                 lambda: ops.gemm_layernorm(self.attn, w["w_o"], w["ln1_w"], w["ln1_b"], bias=w["b_o"], residual=x,
+                                            eps=self.eps, out=self.x1)),
+                ("ffn1", lambda: ops.gemm(self.x1, w["w_1"], self.f, bias=w["b_1"], activation=self.ffn_activation,
+                                          b_layout="nk", **self._tile("ffn1"))),
+                ("ffn2+layernorm_ffn",
+                 lambda: ops.gemm_layernorm(self.f, w["w_2"], w["ln2_w"], w["ln2_b"], bias=w["b_2"],
+                                            residual=self.x1, eps=self.eps, out=y)),
+            ])
         return OrderedDict([
             ("qkv_proj", lambda: ops.gemm(x, w["w_qkv"], self.qkv, bias=w["b_qkv"], b_layout="nk",
                                           **self._tile("qkv_proj"))),
@@ -131,9 +160,9 @@ class EncoderStack:
 
     def __init__(self, layers: List[Dict[str, torch.Tensor]], batch: int, seq: int, num_heads: int = 12,
                  dtype: torch.dtype = torch.float16, device: Optional[torch.device] = None,
-                 eps: float = 1e-5, ffn_activation: str = "gelu_tanh"):
-        self.blocks = [EncoderBlock(w, batch, seq, num_heads, dtype, device, eps, ffn_activation)
-                       for w in layers]
+                 eps: float = 1e-5, ffn_activation: str = "gelu_tanh", fuse_layernorm: bool = True):
+        self.blocks = [EncoderBlock(w, batch, seq, num_heads, dtype, device, eps, ffn_activation,
+                                    fuse_layernorm=fuse_layernorm) for w in layers]
         # Share activation buffers between layers: only the weights differ.
         first = self.blocks[0]
         for blk in self.blocks[1:]:

@@ -104,6 +104,50 @@ def gemm(A: torch.Tensor, B: torch.Tensor, C: Optional[torch.Tensor] = None,
     return C
 
 
+def gemm_layernorm(A: torch.Tensor, B: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor,
+                   bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
+                   eps: float = 1e-5, b_layout: str = "nk", out: Optional[torch.Tensor] = None,
+                   block_n: int = 0, stages: int = 0, num_ctas: int = 0) -> torch.Tensor:
+    """LayerNorm(A @ B + bias + residual) * gamma + beta over the last dimension, in one
+    kernel (lunara_gemm_layernorm). Shapes the fused kernel does not take (N not a
+    multiple of 128/192/256 in 2..8 slices, fp32, unaligned views) run the GEMM into a
+    temporary and the LayerNorm kernel after it -- two launches, same result."""
+    _require_cuda(A, B, gamma, beta, bias, residual, out)
+    assert A.dim() == 2 and B.dim() == 2, "GEMM operands must be 2-D"
+    M, K = A.shape
+    if b_layout == "kn":
+        K2, N = B.shape
+        layout = _lib.B_KN
+    elif b_layout == "nk":
+        N, K2 = B.shape
+        layout = _lib.B_NK
+    else:
+        raise ValueError(f"b_layout must be 'kn' or 'nk', got {b_layout!r}")
+    assert K == K2, f"Dimension mismatch: A{(M, K)} B{tuple(B.shape)}"
+    assert gamma.numel() == N and beta.numel() == N, "gamma/beta must have N elements"
+    if out is None:
+        out = torch.empty(M, N, dtype=A.dtype, device=A.device)
+    assert out.shape == (M, N) and out.dtype == A.dtype and out.stride(1) == 1, "out must be [M, N]"
+    g = gamma.contiguous().to(A.dtype)
+    b = beta.contiguous().to(A.dtype)
+    ldr = 0
+    if residual is not None:
+        assert residual.shape == (M, N) and residual.dtype == A.dtype and residual.stride(1) == 1
+        ldr = residual.stride(0)
+    if bias is not None:
+        assert bias.numel() == N and bias.is_contiguous() and bias.dtype == A.dtype, "bias must be [N], contiguous"
+    lib = _lib.load()
+    rc = lib.lunara_gemm_layernorm(A.data_ptr(), B.data_ptr(), out.data_ptr(), _ptr(bias), _ptr(residual),
+                                   g.data_ptr(), b.data_ptr(), M, N, K, max(A.stride(0), K), max(B.stride(0), 1),
+                                   max(out.stride(0), N), ldr, layout, _dtype_code(A), float(eps),
+                                   _lib.GemmConfig(block_n, stages, num_ctas, 0), _stream())
+    if rc == _lib.ERR_UNSUPPORTED:
+        h = gemm(A, B, bias=bias, residual=residual, b_layout=b_layout)
+        return layernorm(h, g, b, eps, out=out)
+    _lib.check(rc)
+    return out
+
+
 # ────────────────────────────────────────────────────────── attention ──
 
 def attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, causal: bool = False,

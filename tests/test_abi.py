@@ -35,7 +35,7 @@ def test_library_loads_without_gpu():
 def test_exports_every_declared_symbol():
     lib = _lib.load()
     declared = header_functions()
-    assert len(declared) == 15
+    assert len(declared) == 16
     for name in declared:
         assert hasattr(lib, name), name
     assert sorted(_lib.SIGNATURES) == declared
@@ -92,6 +92,12 @@ def _err(lib):
     (lambda L: L.lunara_gemm(1, 1, 1, None, None, 4, 8, 4, 2, 8, 8, 0, 0, 0, 0, None, None), "lda"),
     (lambda L: L.lunara_gemm(1, 1, 1, None, None, -1, 8, 4, 4, 8, 8, 0, 0, 0, 0, None, None), "negative"),
     (lambda L: L.lunara_layernorm(1, 1, 1, 1, 4, 0, 1e-5, 0, None), "shape"),
+    (lambda L: L.lunara_gemm_layernorm(1, 1, 1, None, None, 1, 1, 4, 768, 8, 8, 8, 768, 0, 1, 0, -1.0, None, None),
+     "eps"),
+    (lambda L: L.lunara_gemm_layernorm(1, 1, 1, None, None, None, 1, 4, 768, 8, 8, 8, 768, 0, 1, 0, 1e-5, None,
+                                       None), "NULL"),
+    (lambda L: L.lunara_gemm_layernorm(1, 1, 1, None, None, 1, 1, 4, 100, 8, 8, 8, 100, 0, 1, 0, 1e-5, None, None),
+     "run lunara_gemm then lunara_layernorm"),
     (lambda L: L.lunara_layernorm(1, 1, 1, 1, 4, 8, -1.0, 0, None), "eps"),
     (lambda L: L.lunara_softmax(1, 1, 4, 8, 3, None), "dtype"),
     (lambda L: L.lunara_eltwise_unary(42, 1, 1, 8, 0, None), "op"),

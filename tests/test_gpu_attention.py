@@ -114,3 +114,21 @@ def test_attention_deterministic_and_no_device_error():
     o2 = ops.attention(q.cuda(), k.cuda(), v.cuda())
     assert torch.equal(o1, o2)
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_nan_score_poisons_its_rows_only(dtype, causal):
+    """A NaN in one key makes every score against it NaN: the softmax of each row that
+    sees that key is NaN (as torch's is), whichever pipe computed its exponential; rows
+    that do not see it (causal, earlier queries) and other heads stay finite and exact."""
+    q, k, v = _qkv(1, 2, 384, 384, 64, dtype, 77)
+    k[0, 0, 200, 5] = float("nan")
+    o = _ops().attention(q.cuda(), k.cuda(), v.cuda(), causal=causal).float().cpu()
+    first = 200 if causal else 0
+    assert torch.isnan(o[0, 0, first:]).all(dim=-1).all()
+    assert torch.isfinite(o[0, 0, :first]).all() and torch.isfinite(o[0, 1]).all()
+    ref = oracle.attention(q, k, v, causal)
+    check_close(o[0, 1], ref[0, 1], dtype, "head without the NaN")
+    if causal:
+        check_close(o[0, 0, :first], ref[0, 0, :first], dtype, "rows before the NaN key")

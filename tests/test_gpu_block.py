@@ -13,15 +13,16 @@ def _half_roundtrip(w):
     return {k: v.half().float() for k, v in w.items()}
 
 
-def test_encoder_block_benchmark_config():
+@pytest.mark.parametrize("fuse_layernorm", [True, False])
+def test_encoder_block_benchmark_config(fuse_layernorm):
     from lunara_b200.runtime.encoder import EncoderBlock, GraphRunner
     x, w = inputs.block_inputs(8, 512, seed=0)
     xh, wh = x.half(), _half_roundtrip(w)
     ref = oracle.encoder_block(xh.float(), wh, num_heads=12)
-    blk = EncoderBlock(w, batch=8, seq=512, num_heads=12)
+    blk = EncoderBlock(w, batch=8, seq=512, num_heads=12, fuse_layernorm=fuse_layernorm)
     blk.x.copy_(xh.view(8 * 512, 768).cuda())
     y = blk.run_kernels().clone()
-    check_close(y.view(8, 512, 768), ref, torch.float16, "encoder block (eager)")
+    check_close(y.view(8, 512, 768), ref, torch.float16, f"encoder block (eager, fused LN {fuse_layernorm})")
     runner = GraphRunner(blk.run_kernels)
     y2 = runner.replay()
     torch.cuda.synchronize()

@@ -28,7 +28,7 @@ def _run(x: torch.Tensor, pair: int) -> torch.Tensor:
     return y
 
 
-@pytest.mark.parametrize("pair", [0, 1])
+@pytest.mark.parametrize("pair", [0, 1, 2])
 def test_ex2_poly_relative_error(pair):
     g = torch.Generator().manual_seed(13)
     dense = torch.linspace(-125.0, 8.0, 1 << 20, dtype=torch.float32)
@@ -48,6 +48,16 @@ def test_ex2_poly_relative_error(pair):
 def test_ex2_poly_pair_equals_scalar():
     x = (torch.rand(1 << 16, generator=torch.Generator().manual_seed(14)) * 134.0 - 126.0).cuda()
     assert torch.equal(_run(x, 0).view(torch.int32), _run(x, 1).view(torch.int32))
+    # on [-126, 8] the clamped form the softmax runs is the same function
+    assert torch.equal(_run(x, 1).view(torch.int32), _run(x, 2).view(torch.int32))
+
+
+def test_ex2_poly_clamped_form_below_range():
+    """The softmax's clamped form gives a tiny non-negative value below -126 (-inf included);
+    the softmax zeroes masked columns itself where bf16 would keep it."""
+    below = torch.tensor([-126.5, -200.0, float("-inf"), -1.0e30], dtype=torch.float32).cuda()
+    y = _run(below, 2).cpu()
+    assert torch.isfinite(y).all() and (y >= 0).all() and (y <= 2.0 ** -125).all(), y
 
 
 @pytest.mark.parametrize("pair", [0, 1])
