@@ -10,9 +10,11 @@
 // tile's Q and key blocks load while the current tile finishes.
 //   warps 0-3   softmax warpgroup 0 (thread = query row), half 0
 //   warps 4-7   softmax warpgroup 1 (same rows), half 1
-//   warp 8      TMA producer: Q tiles into a 2-deep buffer, K and V [128 x 64]
-//               blocks into a 4-deep ring (128-byte swizzle, 4-D tensor maps
-//               over the caller's strides, so a fused QKV buffer is read in place)
+//   warp 8      TMA producers: lane 0 loads Q tiles into a 2-deep buffer and
+//               K [128 x 64] blocks into a 4-deep ring, lane 1 loads V blocks
+//               into their own 4-deep ring (128-byte swizzle, 4-D tensor maps
+//               over the caller's strides, so a fused QKV buffer is read in
+//               place); K never waits behind a V slot that a late PV holds
 //   warps 9-10  tcgen05.mma issuers, one per half (warp 9 also allocates TMEM)
 //                 S_w = Q K_j^T     (M=128, N=128, K=64; A, B from shared memory)
 //                 O_w += P_w V_j    (M=128, N=64, K=128; A = P_w from TMEM)
@@ -188,13 +190,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (warp == 8) {
     reg_dealloc<kProducerRegs>();
     if (lane == 0) {
-      // -------------------------------------------------------- TMA producer --
-      // Per work item: its Q tile into the free Q buffer, then its key blocks
-      // into the K/V ring (ring slots and phases count blocks across items).
+      // ------------------------------------------------- TMA producer: Q, K --
+      // Per work item: its Q tile into the free Q buffer, then its key blocks'
+      // K tiles into the K ring (ring slots and phases count blocks across
+      // items). K runs ahead on its own: a K slot frees as soon as the S MMA
+      // that read it completes, so the next S never waits behind a V slot.
       tma_prefetch_desc(&tq);
       tma_prefetch_desc(&tk);
-      tma_prefetch_desc(&tv);
-      int issued_q = 0, issued_kv = 0, issued_v = 0;
+      int issued_q = 0, issued_k = 0;
       bool ok = true;
       for (int k = 0; ok; ++k) {
         const int t = attn_tile_index(k, cta, G);
@@ -209,13 +212,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tma_load_4d(sQ + buf * kTileBytes, &tq, &q_full[buf], 0, x.q0, x.h, x.b);
         ++issued_q;
         for (int j = 0; j < x.nb; ++j) {
-          const int g = issued_kv;
+          const int g = issued_k;
           const int st = g % kKvStages;
           const uint32_t ph = static_cast<uint32_t>(g / kKvStages) & 1u;
           if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, err, kErrAttnProducer)) { ok = false; break; }
           mbar_arrive_expect_tx(&k_full[st], kTileBytes);
           tma_load_4d(sK + st * kTileBytes, &tk, &k_full[st], 0, j * kKvBlock, x.h, x.b);
-          ++issued_kv;
+          ++issued_k;
+        }
+      }
+      if (!ok) {
+        for (int i = (issued_q > 2 ? issued_q - 2 : 0); i < issued_q; ++i)
+          mbar_drain_wait(&q_full[i & 1], static_cast<uint32_t>(i >> 1) & 1u, 1000000000ull);
+        for (int i = (issued_k > kKvStages ? issued_k - kKvStages : 0); i < issued_k; ++i)
+          mbar_drain_wait(&k_full[i % kKvStages], static_cast<uint32_t>(i / kKvStages) & 1u, 1000000000ull);
+      }
+    } else if (lane == 1) {
+      // ---------------------------------------------------- TMA producer: V --
+      // The same walk over work items and key blocks, V tiles into the V ring.
+      tma_prefetch_desc(&tv);
+      int issued_v = 0;
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int t = attn_tile_index(k, cta, G);
+        if (t >= n_tiles) break;
+        const AttnTile x = attn_tile(t, p);
+        for (int j = 0; j < x.nb; ++j) {
+          const int g = issued_v;
+          const int st = g % kKvStages;
+          const uint32_t ph = static_cast<uint32_t>(g / kKvStages) & 1u;
           if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, err, kErrAttnProducer)) { ok = false; break; }
           mbar_arrive_expect_tx(&v_full[st], kTileBytes);
           tma_load_4d(sV + st * kTileBytes, &tv, &v_full[st], 0, j * kKvBlock, x.h, x.b);
@@ -223,10 +248,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
       if (!ok) {
-        for (int i = (issued_q > 2 ? issued_q - 2 : 0); i < issued_q; ++i)
-          mbar_drain_wait(&q_full[i & 1], static_cast<uint32_t>(i >> 1) & 1u, 1000000000ull);
-        for (int i = (issued_kv > kKvStages ? issued_kv - kKvStages : 0); i < issued_kv; ++i)
-          mbar_drain_wait(&k_full[i % kKvStages], static_cast<uint32_t>(i / kKvStages) & 1u, 1000000000ull);
         for (int i = (issued_v > kKvStages ? issued_v - kKvStages : 0); i < issued_v; ++i)
           mbar_drain_wait(&v_full[i % kKvStages], static_cast<uint32_t>(i / kKvStages) & 1u, 1000000000ull);
       }
@@ -549,35 +570,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const float c0 = a0 * inv_l, c1 = a1 * inv_l;
       const uint32_t col = static_cast<uint32_t>(w * 32);
       T* out = static_cast<T*>(p.O) + x.b * p.os_b + x.h * p.os_h + static_cast<int64_t>(qrow) * p.os_s + col;
-      // Two rounds of 16 columns keep the merge's register footprint small.
+      // All four TMEM loads (both halves' O, this warpgroup's 32 columns) are
+      // issued together and waited for once.
+      uint32_t o0[32], o1[32];
 #pragma unroll
-      for (int hcol = 0; hcol < 2; ++hcol) {
-        uint32_t o0[16], o1[16];
+      for (int e = 0; e < 32; ++e) o0[e] = o1[e] = 0u;
+      if (has0) tmem_ld_32x32b_x32(tmem_base + lane_off + kTmemO + col, o0);
+      if (has1) tmem_ld_32x32b_x32(tmem_base + lane_off + kTmemO + kHeadDim + col, o1);
+      tmem_ld_wait_regs(o0);
+      reg_fence(o1);
+      // Both O buffers read: the next item's first P V may overwrite them.
+      tc_fence_before();
+      mbar_arrive(o_free);
+      if (qrow < p.Sq) {
+        uint4* ov4 = reinterpret_cast<uint4*>(out);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) o0[e] = o1[e] = 0u;
-        if (has0) tmem_ld_32x32b_x16(tmem_base + lane_off + kTmemO + col + hcol * 16, o0);
-        if (has1) tmem_ld_32x32b_x16(tmem_base + lane_off + kTmemO + kHeadDim + col + hcol * 16, o1);
-        tmem_ld_wait_regs16(o0, o1);
-        if (hcol == 1) {
-          // Both O buffers read: the next item's first P V may overwrite them.
-          tc_fence_before();
-          mbar_arrive(o_free);
-        }
-        if (qrow < p.Sq) {
-          uint4* ov4 = reinterpret_cast<uint4*>(out + hcol * 16);
+        for (int q = 0; q < 4; ++q) {
+          float f[8];
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            float f[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              f[e] = __uint_as_float(o0[8 * q + e]) * c0 + __uint_as_float(o1[8 * q + e]) * c1;
-            uint4 u;
-            u.x = Io<T>::pack2(f[0], f[1]);
-            u.y = Io<T>::pack2(f[2], f[3]);
-            u.z = Io<T>::pack2(f[4], f[5]);
-            u.w = Io<T>::pack2(f[6], f[7]);
-            ov4[q] = u;
-          }
+          for (int e = 0; e < 8; ++e)
+            f[e] = __uint_as_float(o0[8 * q + e]) * c0 + __uint_as_float(o1[8 * q + e]) * c1;
+          uint4 u;
+          u.x = Io<T>::pack2(f[0], f[1]);
+          u.y = Io<T>::pack2(f[2], f[3]);
+          u.z = Io<T>::pack2(f[4], f[5]);
+          u.w = Io<T>::pack2(f[6], f[7]);
+          ov4[q] = u;
         }
       }
       gi += my_nb;
