@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else if (warp == 9 || warp == 10) {
     reg_dealloc<kProducerRegs>();
-    if (lane == 0) {
+    {
       // ------------------------------------------------------ MMA issuers --
       // Warp 9 + w issues the MMAs of half w, for its key blocks j = w + 2i of
       // each work item: S_w(next) as soon as the softmax has pulled the current
@@ -262,7 +262,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // current block), then P_w V_j once P_w is in TMEM. A ring stage holds
       // one key block and is released by the issuer of the half that uses it;
       // a Q buffer is released by both issuers after their last S of the item.
+      // The whole warp runs the loop (every lane waits and the outcomes are
+      // combined, so all values stay warp-uniform) and one elected lane issues
+      // each MMA and commit.
       const int w = warp - 9;
+      const bool leader = elect_one_sync();
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return mbar_wait_warp(bar, parity, abort_flag, err, kErrAttnMma);
+      };
       constexpr uint64_t kTileStep = kTileBytes >> 4;
       // Descriptors are built once; the start-address field (bits 0-13, in
       // 16-byte units) then moves by constants: +32 B per K step within a
@@ -295,12 +302,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const AttnTile x = attn_tile(t, p);
         const int nbw = w ? x.nb / 2 : (x.nb + 1) / 2;
         const int buf = k & 1;
-        if (!mbar_wait(&q_full[buf], static_cast<uint32_t>(k >> 1) & 1u, abort_flag, err, kErrAttnMma)) {
+        if (!wait(&q_full[buf], static_cast<uint32_t>(k >> 1) & 1u)) {
           ok = false;
           break;
         }
         if (nbw == 0) {
-          mbar_arrive(&q_empty[buf]);
+          if (leader) mbar_arrive(&q_empty[buf]);
+          __syncwarp();
           gb_base += x.nb;
           continue;
         }
@@ -308,61 +316,68 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint64_t qd = qd0 + buf * kTileStep;
         {
           const int g = gb_base + w;
-          if (!mbar_wait(&k_full[g % kKvStages], static_cast<uint32_t>(g / kKvStages) & 1u, abort_flag, err,
-                         kErrAttnMma)) {
+          if (!wait(&k_full[g % kKvStages], static_cast<uint32_t>(g / kKvStages) & 1u)) {
             ok = false;
             break;
           }
-          if (gi > 0 && !mbar_wait(&s_free[w], static_cast<uint32_t>(gi - 1) & 1u, abort_flag, err, kErrAttnMma)) {
+          if (gi > 0 && !wait(&s_free[w], static_cast<uint32_t>(gi - 1) & 1u)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_s(qd, g % kKvStages);
-          umma_commit(&s_full[w]);
-          umma_commit(&k_empty[g % kKvStages]);
-          if (nbw == 1) umma_commit(&q_empty[buf]);
+          if (leader) {
+            issue_s(qd, g % kKvStages);
+            umma_commit(&s_full[w]);
+            umma_commit(&k_empty[g % kKvStages]);
+            if (nbw == 1) umma_commit(&q_empty[buf]);
+          }
+          __syncwarp();
         }
         for (int i = 0; i < nbw && ok; ++i) {
           const int g = gb_base + w + 2 * i;
           const uint32_t cpar = static_cast<uint32_t>(gi + i) & 1u;
           if (i + 1 < nbw) {
             const int gn = g + 2;
-            if (!mbar_wait(&k_full[gn % kKvStages], static_cast<uint32_t>(gn / kKvStages) & 1u, abort_flag, err,
-                           kErrAttnMma)) {
+            if (!wait(&k_full[gn % kKvStages], static_cast<uint32_t>(gn / kKvStages) & 1u)) {
               ok = false;
               break;
             }
-            if (!mbar_wait(&s_free[w], cpar, abort_flag, err, kErrAttnMma)) { ok = false; break; }
+            if (!wait(&s_free[w], cpar)) { ok = false; break; }
             tc_fence_after();
-            issue_s(qd, gn % kKvStages);
-            umma_commit(&s_full[w]);
-            umma_commit(&k_empty[gn % kKvStages]);
-            if (i + 2 == nbw) umma_commit(&q_empty[buf]);
+            if (leader) {
+              issue_s(qd, gn % kKvStages);
+              umma_commit(&s_full[w]);
+              umma_commit(&k_empty[gn % kKvStages]);
+              if (i + 2 == nbw) umma_commit(&q_empty[buf]);
+            }
+            __syncwarp();
           }
           const int st = g % kKvStages;
-          if (!mbar_wait(&v_full[st], static_cast<uint32_t>(g / kKvStages) & 1u, abort_flag, err, kErrAttnMma)) {
+          if (!wait(&v_full[st], static_cast<uint32_t>(g / kKvStages) & 1u)) {
             ok = false;
             break;
           }
-          if (!mbar_wait(&p_ready[w], cpar, abort_flag, err, kErrAttnMma)) { ok = false; break; }
+          if (!wait(&p_ready[w], cpar)) { ok = false; break; }
           // The first P V of an item overwrites O_w: the previous item's merge
           // must have read it.
-          if (i == 0 && k > 0 &&
-              !mbar_wait(o_free, static_cast<uint32_t>(k - 1) & 1u, abort_flag, err, kErrAttnMma)) {
+          if (i == 0 && k > 0 && !wait(o_free, static_cast<uint32_t>(k - 1) & 1u)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_pv(st, i == 0);
-          umma_commit(&o_full[w]);
-          umma_commit(&v_empty[st]);
+          if (leader) {
+            issue_pv(st, i == 0);
+            umma_commit(&o_full[w]);
+            umma_commit(&v_empty[st]);
+          }
+          __syncwarp();
         }
         gi += nbw;
         gb_base += x.nb;
       }
       if (!ok) {
-        umma_commit(&drain_bar[w]);
+        if (leader) umma_commit(&drain_bar[w]);
+        __syncwarp();
         mbar_drain_wait(&drain_bar[w], 0, 1000000000ull);
       }
     }

@@ -123,6 +123,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// The bounded wait above for a warp that runs warp-uniform control flow:
+// every lane waits and the outcomes are combined, so all lanes take the same
+// branch. (Lane 0 waiting alone with its outcome broadcast by a shuffle
+// measured slower on B200, in the attention and the GEMM issuers alike.)
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                               unsigned int* err, unsigned int site) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, err, site));
+}
+
 // Wait used while draining after an abort: bounded, never sets the flag.
 __device__ __forceinline__ void mbar_drain_wait(uint64_t* bar, uint32_t parity, unsigned long long budget_ns) {
   const unsigned long long t0 = globaltimer_ns();
@@ -219,6 +228,19 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// Elects one lane of the fully active warp (elect.sync); true on that lane only.
+// An MMA-issuing warp runs its loop on all lanes, so the descriptors and
+// counters it carries are warp-uniform, and only the elected lane issues.
+__device__ __forceinline__ bool elect_one_sync() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
 }
 
 // Arrive once on the mbarrier when every tcgen05 op issued so far by this thread has completed.

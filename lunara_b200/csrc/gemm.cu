@@ -406,40 +406,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {
       // ------------------------------------------------------- MMA issuer --
+      // The whole warp runs the loop (every lane waits, the outcomes combined),
+      // so its counters and descriptors stay warp-uniform; one elected lane
+      // issues the MMAs and commits.
+      const bool elected = elect_one_sync();
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, err, kErrGemmMma)) {
+        if (!mbar_wait_warp(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, err, kErrGemmMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * ACC_STRIDE;
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, abort_flag, err, kErrGemmMma)) {
+          if (!mbar_wait_warp(&full_bar[stage], phase, abort_flag, err, kErrGemmMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
           const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+          uint64_t ad[BK / 16], bd[BK / 16];
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = sw128_desc(a_addr + k * 32, 16, 1024);
-            const uint64_t bd = B_KMAJOR ? sw128_desc(b_addr + k * 32, 16, 1024)
-                                         : sw128_desc(b_addr + k * 2048, BK * 128, 1024);
-            umma_f16_ss(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+            ad[k] = sw128_desc(a_addr + k * 32, 16, 1024);
+            bd[k] = B_KMAJOR ? sw128_desc(b_addr + k * 32, 16, 1024) : sw128_desc(b_addr + k * 2048, BK * 128, 1024);
           }
-          umma_commit(&empty_bar[stage]);
+          if (elected) {
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) umma_f16_ss(d_tmem, ad[k], bd[k], IDESC, (kb | k) != 0 ? 1u : 0u);
+            umma_commit(&empty_bar[stage]);
+          }
+          __syncwarp();
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull_bar[acc]);
+        if (elected) umma_commit(&tfull_bar[acc]);
+        __syncwarp();
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
@@ -447,7 +456,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (!ok) {
         // Wait for the MMAs already issued before TMEM is released.
-        umma_commit(drain_bar);
+        if (elected) umma_commit(drain_bar);
+        __syncwarp();
         mbar_drain_wait(drain_bar, 0, 1000000000ull);
       }
     }
@@ -634,47 +644,55 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && leader) {
+    if (leader) {
       // ------------------------------------------------ MMA issuer (pair) --
+      // Warp-uniform loop, elected lane issues (as in the single-CTA kernel).
+      const bool elected = elect_one_sync();
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
       for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
-        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, err, kErrGemmMma)) {
+        if (!mbar_wait_warp(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, err, kErrGemmMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * ACC_STRIDE;
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, abort_flag, err, kErrGemmMma)) {
+          if (!mbar_wait_warp(&full_bar[stage], phase, abort_flag, err, kErrGemmMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
           const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+          uint64_t ad[BK / 16], bd[BK / 16];
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = sw128_desc(a_addr + k * 32, 16, 1024);
-            const uint64_t bd = B_KMAJOR ? sw128_desc(b_addr + k * 32, 16, 1024)
-                                         : sw128_desc(b_addr + k * 2048, BK * 128, 1024);
-            umma_f16_ss_pair(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+            ad[k] = sw128_desc(a_addr + k * 32, 16, 1024);
+            bd[k] = B_KMAJOR ? sw128_desc(b_addr + k * 32, 16, 1024) : sw128_desc(b_addr + k * 2048, BK * 128, 1024);
           }
-          umma_commit_pair(&empty_bar[stage], 0x3);
+          if (elected) {
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) umma_f16_ss_pair(d_tmem, ad[k], bd[k], IDESC, (kb | k) != 0 ? 1u : 0u);
+            umma_commit_pair(&empty_bar[stage], 0x3);
+          }
+          __syncwarp();
           if (++stage == static_cast<uint32_t>(STAGES)) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit_pair(&tfull_bar[acc], 0x3);
+        if (elected) umma_commit_pair(&tfull_bar[acc], 0x3);
+        __syncwarp();
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
         }
       }
       if (!ok) {
-        umma_commit_pair(drain_bar, 0x1);
+        if (elected) umma_commit_pair(drain_bar, 0x1);
+        __syncwarp();
         mbar_drain_wait(drain_bar, 0, 1000000000ull);
       }
     }
@@ -1143,47 +1161,57 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {
       // ------------------------------------------------------- MMA issuer --
+      // The whole warp runs the loop (every lane waits, the outcomes combined),
+      // so its counters and descriptors stay warp-uniform; one elected lane
+      // issues the MMAs and commits.
+      const bool elected = elect_one_sync();
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
       for (int tile = cid; ok && tile < m_tiles; tile += ncl) {
-        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, err, kErrGemmMma)) {
+        if (!mbar_wait_warp(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, err, kErrGemmMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * ACC_STRIDE;
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, abort_flag, err, kErrGemmMma)) {
+          if (!mbar_wait_warp(&full_bar[stage], phase, abort_flag, err, kErrGemmMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
           const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+          uint64_t ad[BK / 16], bd[BK / 16];
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = sw128_desc(a_addr + k * 32, 16, 1024);
-            const uint64_t bd = B_KMAJOR ? sw128_desc(b_addr + k * 32, 16, 1024)
-                                         : sw128_desc(b_addr + k * 2048, BK * 128, 1024);
-            umma_f16_ss(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+            ad[k] = sw128_desc(a_addr + k * 32, 16, 1024);
+            bd[k] = B_KMAJOR ? sw128_desc(b_addr + k * 32, 16, 1024) : sw128_desc(b_addr + k * 2048, BK * 128, 1024);
           }
-          umma_commit(&empty_bar[stage]);
+          if (elected) {
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) umma_f16_ss(d_tmem, ad[k], bd[k], IDESC, (kb | k) != 0 ? 1u : 0u);
+            umma_commit(&empty_bar[stage]);
+          }
+          __syncwarp();
           if (++stage == static_cast<uint32_t>(STAGES)) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull_bar[acc]);
+        if (elected) umma_commit(&tfull_bar[acc]);
+        __syncwarp();
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
         }
       }
       if (!ok) {
-        umma_commit(drain_bar);
+        if (elected) umma_commit(drain_bar);
+        __syncwarp();
         mbar_drain_wait(drain_bar, 0, 1000000000ull);
       }
     }
