@@ -840,8 +840,8 @@ bool encode_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, ui
 // the pair's epilogue hand-off): fitted to a sweep of 12 shapes on B200
 // (block, 12-layer-stack and square GEMMs), where, with the one-round rate
 // below, it picks the fastest plan or one within 2% for every shape
-// (single-CTA 128x192 tiles for N=768 outputs of 4096 rows, CTA pairs for
-// wide N and for many rounds).
+// (single-CTA 128x192 tiles for N=768 outputs of 4096 rows at K=768, 256x192
+// CTA pairs at K=3072, CTA pairs for wide N and for many rounds).
 struct GemmPlan {
   int block_n;
   bool pair;
@@ -852,10 +852,11 @@ double gemm_cost(int64_t M, int64_t N, int64_t K, GemmPlan p, int sms) {
   const int64_t tiles = ceil_div64(M, tile_m) * ceil_div64(N, p.block_n);
   const int64_t units = p.pair ? sms / 2 : sms;
   const int64_t rounds = ceil_div64(tiles, units);
-  // Single-CTA tiles that all fit in one round stream their operands at a
-  // higher rate than the all-SMs-busy figure (measured: 4096x768 at K=768 and
-  // K=3072, 2048^3), so they are costed at 80 B/cycle instead of 60.
-  const double l2_bytes_per_cycle = (!p.pair && rounds == 1) ? 80.0 : 60.0;
+  // Tiles that all fit in one round stream their operands at a higher rate
+  // than the all-SMs-busy figure (measured: single-CTA 4096x768 at K=768 and
+  // K=3072, 2048^3; CTA pairs with a 5-stage ring, 4096x768 at K=3072), so they
+  // are costed at 80 B/cycle instead of 60.
+  const double l2_bytes_per_cycle = (rounds == 1) ? 80.0 : 60.0;
   const double bytes = BM * BK * 2.0 + (p.pair ? p.block_n / 2 : p.block_n) * BK * 2.0;
   const double per_kb = std::max(2.0 * p.block_n, bytes / l2_bytes_per_cycle);
   return static_cast<double>(rounds) * (static_cast<double>(ceil_div64(K, BK)) * per_kb + (p.pair ? 3200.0 : 0.0));
@@ -909,9 +910,11 @@ cudaError_t run_tc2(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap&
   constexpr int kStageBytes = BM * BK * 2 + (BN / 2) * BK * 2;
   static_assert(kMaxStages * kStageBytes + kSmemReserve <= kMaxDynSmem, "shared memory budget");
   // Default ring depth: the deepest that fits, except for 192-wide tiles, where
-  // 4 stages measured faster on B200 than the 7 that fit (4096 x 768 outputs,
-  // K = 768 and 3072: 11.1 vs 12.3 us and 21.5 vs 22.5 us).
-  constexpr int kDefaultStages = (BN == 192 && kMaxStages > 4) ? 4 : kMaxStages;
+  // 5 stages measured fastest on B200 of the 3 to 7 that fit (4096 x 768
+  // outputs; K = 3072 inside the encoder block step: 98.1 / 95.2 / 95.3 / 95.3 us
+  // with 4 / 5 / 6 / 7 stages; K = 768 alone with cold operands: 11.8 / 11.3 /
+  // 12.0 us with 4 / 5 / 7).
+  constexpr int kDefaultStages = (BN == 192 && kMaxStages > 5) ? 5 : kMaxStages;
   const int stages = (g.stages >= 2 && g.stages <= kMaxStages) ? g.stages : kDefaultStages;
   const int smem = stages * kStageBytes + kSmemReserve;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
