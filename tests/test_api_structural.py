@@ -301,3 +301,16 @@ def test_parse_ncu_csv(tmp_path):
 def test_print_summary_handles_empty(capsys):
     NsightProfiler.print_summary(ProfileResult())
     assert "Profile Summary" in capsys.readouterr().out
+
+
+def test_encoder_block_form_by_tokens_per_block():
+    """The encoder block runs the reference's seven kernels below FUSE_LAYERNORM_MIN_TOKENS
+    tokens per block (the benchmark's B8 S512 block, a rank's share of the 8-GPU stack) and
+    the five-kernel fused-LayerNorm form from there up (the 12-layer B64 stack on one GPU)."""
+    from lunara_b200.runtime import encoder as enc
+    assert enc.FUSE_LAYERNORM_MIN_TOKENS == 16384
+    assert not enc.default_fuse_layernorm(8, 512)
+    assert not enc.default_fuse_layernorm(16, 512)
+    assert enc.default_fuse_layernorm(32, 512)
+    assert enc.default_fuse_layernorm(64, 512)
+    assert len(enc.KERNEL_ORDER) == 7 and len(enc.FUSED_KERNEL_ORDER) == 5
